@@ -1,0 +1,406 @@
+"""Benchmark of the EXL3 hot path on B200: decode-regime EXL3 linears (M = 1) of one synthetic
+27B-class decoder layer, as the serving engine calls them (qkv and gate_up as grouped modules).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--bits 4] [--m 1]
+
+One step = one pass over the seven EXL3 linears of one layer (q, k, v as one 3-group call; o;
+gate, up as one 2-group call; down) at M rows.  Steps rotate over layer copies whose total size
+is far above the 126 MB L2, so every step streams its weights from HBM.  value = algorithmic
+bytes (packed codes + suh + svh + x + y) / device time, summed over all ranks' shards.
+
+N > 1: tensor parallel over N ranks (one process per GPU, NCCL): q/k/v/gate/up column-parallel
+(n sharded in 128-column blocks), o/down row-parallel (k sharded) followed by an NCCL all-reduce
+of the fp16 output, as vLLM's RowParallelLinear does.  Total work is fixed: scaling "strong".
+
+--impl reference: times the CPU restatement of the reference's oracle (the reference path has no
+GPU implementation that runs here; its kernels are HIP/gfx1201) on the host cores, on a bounded
+sample of the same workload, and reports the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen38-27b-exl3-rdna4_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "EXL3 GEMM HBM GB/s (M=1) & TFLOP/s (M=2048); decode tok/s at 1/2/4/8 B200"
+HIDDEN, INTER, HEADS, KV_HEADS, HEAD_DIM = 5120, 17408, 40, 8, 128
+# (name, k, n, row_parallel) of one decoder layer; q/k/v and gate/up are grouped modules
+LAYER = [("q", HIDDEN, HEADS * HEAD_DIM, False), ("k", HIDDEN, KV_HEADS * HEAD_DIM, False),
+         ("v", HIDDEN, KV_HEADS * HEAD_DIM, False), ("o", HEADS * HEAD_DIM, HIDDEN, True),
+         ("gate", HIDDEN, INTER, False), ("up", HIDDEN, INTER, False), ("down", INTER, HIDDEN, True)]
+MODULES = [("qkv", ["q", "k", "v"]), ("o", ["o"]), ("gate_up", ["gate", "up"]), ("down", ["down"])]
+L2_BYTES = 126 * 1024 * 1024
+
+
+def linear_bytes(k: int, n: int, K: int, m: int) -> int:
+    """Algorithmic bytes of one EXL3 linear: codes + suh + svh + x + y (fp16)."""
+    return k * n * K // 8 + 2 * k + 2 * n + 2 * m * k + 2 * m * n
+
+
+def shard_shape(k, n, row_parallel, tp, rank):
+    if tp == 1:
+        return k, n
+    if row_parallel:
+        assert k % (128 * tp) == 0
+        return k // tp, n
+    assert n % (128 * tp) == 0
+    return k, n // tp
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------
+# synthetic layer weights (seeded uniform codes, random +-1 signs), generated on the device
+# ---------------------------------------------------------------------------------------------
+def make_layer(torch, dev, K, tp, rank, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    out = {}
+    for name, k, n, rowp in LAYER:
+        ks, ns = shard_shape(k, n, rowp, tp, rank)
+        tr = torch.randint(-32768, 32768, (ks // 16, ns // 16, 16 * K), generator=g, device=dev,
+                           dtype=torch.int32).to(torch.int16)
+        suh = (torch.randint(0, 2, (ks,), generator=g, device=dev) * 2 - 1).to(torch.float16)
+        svh = (torch.randint(0, 2, (ns,), generator=g, device=dev) * 2 - 1).to(torch.float16)
+        out[name] = (tr, suh, svh, ks, ns)
+    return out
+
+
+def run_layer(torch, layer, x, inputs, K, tp, pg):
+    """One decoder layer's EXL3 linears as the engine calls them: x feeds qkv and gate_up; the
+    row-parallel o and down read their own (sharded) inputs.  Returns the last output."""
+    ops = torch.ops.exl3rocm
+    y = None
+    for mod, names in MODULES:
+        ts = [layer[nm][0] for nm in names]
+        su = [layer[nm][1] for nm in names]
+        sv = [layer[nm][2] for nm in names]
+        kin = layer[names[0]][3]
+        xin = x if kin == x.shape[1] and mod in ("qkv", "gate_up") else inputs[kin]
+        if len(names) == 1:
+            y = ops.linear(xin, ts[0], su[0], sv[0], K, False, True)
+        else:
+            y = ops.linear_groups(xin, ts, su, sv, [K] * len(names), False, True)
+        if tp > 1 and mod in ("o", "down"):
+            torch.distributed.all_reduce(y, group=pg)
+    return y
+
+
+def layer_bytes(K, m, tp):
+    """Algorithmic bytes of one layer summed over all tp shards."""
+    total = 0
+    for name, k, n, rowp in LAYER:
+        for r in range(tp):
+            ks, ns = shard_shape(k, n, rowp, tp, r)
+            total += linear_bytes(ks, ns, K, m)
+    return total
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline: the oracle restatement on the host cores (bounded sample)
+# ---------------------------------------------------------------------------------------------
+def _cpu_slice(args):
+    k, n_cols, K, seed = args
+    from oracle import exl3_oracle as O
+    rng = np.random.default_rng(seed)
+    tr = O.random_trellis(rng, k // 16, n_cols // 16, K)
+    suh = np.sign(rng.standard_normal(k)).astype(np.float16)
+    svh = np.sign(rng.standard_normal(n_cols)).astype(np.float16)
+    x = rng.standard_normal((1, k)).astype(np.float16)
+    t0 = time.perf_counter()
+    O.linear(x, tr, K, suh, svh, 2)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(K: int, budget_cols: int = 8704) -> dict:
+    """Time the oracle's linear (M=1, mul1) on a column sample of the gate layer, one slice per
+    host core in a spawn pool; report the metric's unit for that sample."""
+    import multiprocessing as mp
+    cores = os.cpu_count() or 1
+    per = max(128, (budget_cols // cores) // 128 * 128)
+    jobs = [(HIDDEN, per, K, 1000 + i) for i in range(cores)]
+    ctx = mp.get_context("spawn")
+    t0 = time.perf_counter()
+    with ctx.Pool(cores) as pool:
+        pool.map(_cpu_slice, jobs)
+    wall = time.perf_counter() - t0
+    # generation of the synthetic codes is inside the slices but outside each slice's timer;
+    # the reported value uses the wall time of the whole pool (generation included: conservative)
+    nbytes = sum(linear_bytes(HIDDEN, per, K, 1) for _ in jobs)
+    return {"value": nbytes / wall / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"oracle linear M=1 mul1 K={K}: {cores} x (5120 x {per}) column slices of gate_proj, "
+                      f"process pool, {wall:.1f} s wall"}
+
+
+# ---------------------------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--bits", type=int, default=4)
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    K, M = args.bits, args.m
+
+    config = {"workload": f"one 27B-class decoder layer's EXL3 linears (qkv, o, gate_up, down), M={M}, "
+                          f"{K} bits, mul1 codebook, x bf16 cast to fp16", "model": "synthetic 27B-class layer",
+              "hidden": HIDDEN, "intermediate": INTER, "m": M, "bits": K, "tp": world,
+              "parallelism": f"tp{world}" if world > 1 else "single", "l2": "weights rotate over copies > 2x L2"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(K)
+        # each "step" of the reference arm is one bounded CPU sample of the workload
+        vals = [cb["value"]]
+        for _ in range(max(0, min(args.steps, 2) - 1)):
+            vals.append(cpu_baseline(K)["value"])
+        v = statistics.median(vals)
+        line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": len(vals),
+                "warmup": 0, "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "fp16", "data": "synthetic", "config": config,
+                "impl": "reference", "cpu_baseline": dict(cb, value=v),
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+        pg = torch.distributed.group.WORLD
+    import exl3rocm.ops  # noqa: F401  registers torch.ops.exl3rocm.*
+    from exl3rocm import ops as xops
+
+    one = layer_bytes(K, M, 1) // 1
+    copies = max(2, int(np.ceil(3 * L2_BYTES * world / max(1, one))))  # per-rank bytes > 3x L2
+    layers = [make_layer(torch, dev, K, world, rank, seed=1234 + 17 * c) for c in range(copies)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    x = torch.randn((M, HIDDEN), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    inputs = {layers[0][nm][3]: torch.randn((M, layers[0][nm][3]), generator=g, device=dev,
+                                           dtype=torch.float32).to(torch.bfloat16) for nm in ("o", "down")}
+
+    # One CUDA graph per layer copy, as a serving engine replays its decode step.  The graphs read
+    # the static input x; e2e refreshes x from pinned host memory and reads y back every step.
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    graphs, outs = [], []
+    with torch.cuda.stream(stream):
+        for lay in layers:
+            for mod, names in MODULES:
+                xops.reserve_workspace(dev, lay[names[0]][3], sum(lay[nm][4] for nm in names), len(names), 16)
+        for i in range(3):
+            run_layer(torch, layers[i % copies], x, inputs, K, world, pg)
+        stream.synchronize()
+        for lay in layers:
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_, stream=stream):
+                outs.append(run_layer(torch, lay, x, inputs, K, world, pg))
+            graphs.append(g_)
+        # gate_up alone, for the per-call roofline of the dominant kernel
+        gu_graphs = []
+        for lay in layers:
+            ts = [lay[nm][0] for nm in ("gate", "up")]
+            su = [lay[nm][1] for nm in ("gate", "up")]
+            sv = [lay[nm][2] for nm in ("gate", "up")]
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_, stream=stream):
+                torch.ops.exl3rocm.linear_groups(x, ts, su, sv, [K, K], False, True)
+            gu_graphs.append(g_)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % copies].replay()
+    torch.cuda.synchronize()
+
+    # ---- device-timed region ----
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk, torch.cuda.stream(stream):
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            graphs[i % copies].replay()
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    ms_per_step = total_ms / args.steps
+    total_bytes = layer_bytes(K, M, world)
+    value = total_bytes / (ms_per_step * 1e-3) / 1e9
+    clocks = clk.summary()
+
+    # ---- per-call timing of the dominant kernel's call (gate_up, the largest), graph-replayed ----
+    lay = layers[0]
+    n_calls = 3 * copies
+    gu_ms = []
+    with torch.cuda.stream(stream):
+        for i in range(n_calls):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            gu_graphs[i % copies].replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            gu_ms.append(e0.elapsed_time(e1))
+    gu_bytes = sum(linear_bytes(lay[nm][3], lay[nm][4], K, M) for nm in ("gate", "up"))
+    gu_ms_med = statistics.median(gu_ms)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = gu_bytes / (gu_ms_med * 1e-3) / 1e9
+
+    # ---- end to end: pinned host x -> device, the layer's ops (graph), y -> pinned host ----
+    x_host = torch.randn((M, HIDDEN), dtype=torch.float32).to(torch.bfloat16).pin_memory()
+    y_host = torch.empty(outs[0].shape, dtype=outs[0].dtype).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e_s.record(stream)
+        for i in range(args.steps):
+            x.copy_(x_host, non_blocking=True)
+            graphs[i % copies].replay()
+            y_host.copy_(outs[i % copies], non_blocking=True)
+        e_e.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = e_s.elapsed_time(e_e)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
+    del graphs, gu_graphs
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(K)
+
+    if world > 1:
+        torch.distributed.barrier(device_ids=[local])
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded uniform trellis codes, +-1 signs, x ~ N(0,1) bf16)", "config": config,
+        "step_ms_median": statistics.median(step_ms),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": None,
+                     "kernel": "gate_up linear_groups call (had_in + gemv_kernel, graph-replayed), median "
+                               f"of {n_calls} event-timed calls, {gu_bytes} algorithmic bytes per call",
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 2),
+                "d2h_bytes_per_step": int(y_host.numel() * 2)},
+        "gpu_launches": args.steps * 2 * len(MODULES),
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

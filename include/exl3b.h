@@ -1,0 +1,114 @@
+/*
+ * exl3b: the EXL3 inference hot path for NVIDIA B200 (sm_100a), as a C ABI.
+ *
+ * Plain C: raw device pointers, sizes, a cudaStream_t passed as void*, and an int status.
+ *   0  EXL3B_OK
+ *   >0 the call was declined (unsupported shape or flags, bad argument, workspace too small);
+ *      nothing was launched and no output was touched
+ *   <0 -(cudaError_t) from a launch; outputs are unspecified
+ * Every call is asynchronous on `stream`, never allocates device memory and never
+ * synchronises, so it may be captured into a CUDA graph.  fp16 tensors are passed as
+ * uint16_t bit patterns.
+ *
+ * Each entry point names the reference interface it replaces (reference repository
+ * Luke458/qwen38-27b-exl3-rdna4; the pybind extension `exllamav3_ext` is the un-vendored
+ * fork CarouselAether/rocm_exl3 @ 311ff5497237a37bea18cf24aa18bc0c573d1d03, whose call
+ * sites are in vllm_plugin/exl3rocm/ops.py and tests/test_gpu_parity.py).
+ */
+#ifndef EXL3B_H
+#define EXL3B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EXL3B_API __attribute__((visibility("default")))
+#else
+#define EXL3B_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXL3B_OK 0
+#define EXL3B_DECLINED 1  /* shape / flags outside what the kernels implement */
+#define EXL3B_BAD_ARG 2   /* null or misaligned pointer, bad size */
+#define EXL3B_WORKSPACE 3 /* workspace smaller than exl3b_linear_workspace_bytes() */
+
+/* codebook ids: the (mcg, mul1) flags of the reference ops map to 0 = 3INST, 1 = MCG, 2 = MUL1
+ * (reference tests/test_gpu_parity.py:101) */
+#define EXL3B_CB_3INST 0
+#define EXL3B_CB_MCG 1
+#define EXL3B_CB_MUL1 2
+
+#define EXL3B_MAX_GROUPS 8
+#define EXL3B_GEMV_MAX_ROWS 16
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+EXL3B_API int exl3b_version(void);
+
+/* Human-readable text for a status code (static storage). */
+EXL3B_API const char* exl3b_status_string(int status);
+
+/* Decode raw 16-bit trellis states through a codebook to fp32 copies of the fp16 values.
+ * Replaces exllamav3_ext.decode(codes, out, mcg, mul1) (reference tests/test_gpu_parity.py:101-109). */
+EXL3B_API int exl3b_decode_states(const uint16_t* states, float* out, int64_t count, int codebook, void* stream);
+
+/* Dequantize ("reconstruct") a trellis [k/16][n/16][16K] into fp16 W[k][ldw], output columns
+ * n0..n1 of the layer written to W columns 0..n1-n0.  Bit-exact to the reference oracle.
+ * Replaces exllamav3_ext.reconstruct(W, B, K, mcg, mul1) and reconstruct_slice(W, B, K, mcg, mul1, n0)
+ * (reference vllm_plugin/exl3rocm/ops.py:92-95). Requires n0, n1 multiples of 16, ldw % 8 == 0. */
+EXL3B_API int exl3b_dequant(const uint16_t* trellis, int k, int n, int K, int codebook, int n0, int n1,
+                  uint16_t* W, int64_t ldw, void* stream);
+
+/* 128-point Hadamard over each 128-column block of a [rows][cols] fp16 matrix:
+ *   out = fp16( H128 * fp16(in * pre) * scale / sqrt(128) ) * post     (pre, post optional)
+ * in == out is allowed.  Replaces exllamav3_ext.had_r_128(in, out, pre, post, scale)
+ * (reference vllm_plugin/exl3rocm/ops.py:88,97). cols % 128 == 0, lds % 4 == 0. */
+EXL3B_API int exl3b_had128(const uint16_t* in, int64_t ld_in, uint16_t* out, int64_t ld_out, int64_t rows, int64_t cols,
+                 const uint16_t* pre, const uint16_t* post, float scale, void* stream);
+
+/* Workspace for exl3b_linear / exl3b_linear_grouped: m rows, k inputs, `groups` weight groups
+ * with n_total (<= 1048576) output columns in all.  The first EXL3B_WS_ZERO_BYTES bytes must be
+ * zero before the first call; every call leaves them zero again, so a workspace allocated once
+ * with zeros can be reused by calls of any shape issued in stream order.  Calls that may run
+ * concurrently need separate workspaces.  After a call that reported a kernel error
+ * (exl3b_linear_workspace_error) the workspace must be zeroed again. */
+#define EXL3B_WS_ZERO_BYTES (256 + 4 * 8192)
+EXL3B_API size_t exl3b_linear_workspace_bytes(int m, int k, int groups, int64_t n_total);
+
+/* The EXL3 linear for 1 <= m <= 16 (decode / speculative verify):
+ *   y[m][n] = had_out( fp16( had_in(x, suh) @ W ), svh )
+ * x fp16 [m][k] contiguous, trellis int16 [k/16][n/16][16K], suh fp16 [k], svh fp16 [n],
+ * y fp16 rows of stride ldy.  k % 128 == 0, n % 128 == 0, 1 <= K <= 8.  Each output row is
+ * bitwise identical to the m = 1 call on that row alone, and repeated calls are bitwise
+ * identical.
+ * Replaces exllamav3_ext.exl3_gemm (m = 1) and exl3_gemv_mr (m <= 16) with their fused input and
+ * output Hadamards (reference vllm_plugin/exl3rocm/ops.py:80-85; multi-row contract
+ * vllm_plugin/patches/exl3-fork/0002-gemv-multirow.patch:79-88). */
+EXL3B_API int exl3b_linear(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K, int codebook,
+                 const uint16_t* suh, const uint16_t* svh, uint16_t* y, int64_t ldy,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Up to EXL3B_MAX_GROUPS weight groups that share the input x and the bit width K (gate/up,
+ * q/k/v), in one launch.  Group i has its own trellis [k/16][n[i]/16][16K], suh[i], svh[i] and
+ * writes y[i] (row stride ldy).  Host arrays of device pointers.  For a fixed set of groups each
+ * output row is bitwise identical to the m = 1 call on that row (the work partition spans the
+ * groups, so it depends on the group set, not on m).
+ * Replaces exllamav3_ext.exl3_mgemm (m = 1) and exl3_gemv_mr_grouped
+ * (reference vllm_plugin/exl3rocm/ops.py:134-170, 0002-gemv-multirow.patch:174-182). */
+EXL3B_API int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis,
+                         const int* n, int K, int codebook, const uint16_t* const* suh,
+                         const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads the kernel error word of a linear workspace (0 = none; otherwise the code of a wait that
+ * gave up) into *out, synchronising `stream`.  Test and diagnostics helper. */
+EXL3B_API int exl3b_linear_workspace_error(const void* workspace, int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3B_H */
