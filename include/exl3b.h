@@ -35,6 +35,7 @@ extern "C" {
 #define EXL3B_DECLINED 1  /* shape / flags outside what the kernels implement */
 #define EXL3B_BAD_ARG 2   /* null or misaligned pointer, bad size */
 #define EXL3B_WORKSPACE 3 /* workspace smaller than exl3b_linear_workspace_bytes() */
+#define EXL3B_TOO_LARGE 4 /* exl3b_linear_noalloc: the call needs more than its static scratch */
 
 /* codebook ids: the (mcg, mul1) flags of the reference ops map to 0 = 3INST, 1 = MCG, 2 = MUL1
  * (reference tests/test_gpu_parity.py:101) */
@@ -102,6 +103,27 @@ EXL3B_API int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, 
                          const int* n, int K, int codebook, const uint16_t* const* suh,
                          const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* exl3b_linear without a caller-provided workspace, for callers that cannot allocate device
+ * memory: code that runs while a CUDA graph is being captured (cudaMalloc is not allowed there),
+ * hosts whose device memory is owned by a pool the caller cannot reach, and latency-critical
+ * paths where cudaMalloc's implicit device synchronisation is unacceptable.  This entry point has
+ * no counterpart in the reference: the reference always receives its scratch from the torch
+ * caching allocator.
+ * Same arguments, results and limits as exl3b_linear (each row bitwise equal to exl3b_linear's),
+ * but the scratch lives in one static device array of EXL3B_NOALLOC_SCRATCH_BYTES (8 MiB) that
+ * every GPU loading this library holds until exit; the call allocates nothing.  Calls whose
+ * workspace (exl3b_linear_workspace_bytes(m, k, 1, n)) exceeds it return EXL3B_TOO_LARGE
+ * before launching anything (m <= 16 with k <= 65536 always fits on a B200).
+ * The first call on a device resolves the array's device address with that device current
+ * (a one-time, synchronous set-up): make it before any stream capture.  Every call clears the
+ * array's counter region on `stream` first, and all calls share the array, so calls that can
+ * overlap on the GPU (different streams, or graphs replayed concurrently) race: issue them in
+ * one stream order. */
+#define EXL3B_NOALLOC_SCRATCH_BYTES (8u << 20)
+EXL3B_API int exl3b_linear_noalloc(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K,
+                                   int codebook, const uint16_t* suh, const uint16_t* svh, uint16_t* y,
+                                   int64_t ldy, void* stream);
 
 /* Reads the kernel error word of a linear workspace (0 = none; otherwise the code of a wait that
  * gave up) into *out, synchronising `stream`.  Test and diagnostics helper. */

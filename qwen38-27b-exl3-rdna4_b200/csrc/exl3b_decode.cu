@@ -153,6 +153,7 @@ extern "C" const char* exl3b_status_string(int status) {
         case EXL3B_DECLINED: return "declined: shape or flags not implemented by the kernels";
         case EXL3B_BAD_ARG: return "bad argument: null or misaligned pointer, or bad size";
         case EXL3B_WORKSPACE: return "workspace too small";
+        case EXL3B_TOO_LARGE: return "call needs more scratch than the static scratch array of exl3b_linear_noalloc holds";
         default: break;
     }
     if (status < 0) return cudaGetErrorString((cudaError_t)(-status));

@@ -377,7 +377,7 @@ static cudaError_t launch_gemv_k(int K, const GemvParams& p, cudaStream_t st) {
     }
 }
 
-static int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis, const int* n,
+int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis, const int* n,
                        int K, int codebook, const uint16_t* const* suh, const uint16_t* const* svh,
                        uint16_t* const* y, int64_t ldy, void* workspace, size_t ws_bytes, void* stream) {
     if (K < 1 || K > 8 || codebook < 0 || codebook > 2) return EXL3B_DECLINED;

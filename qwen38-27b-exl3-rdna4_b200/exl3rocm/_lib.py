@@ -15,6 +15,7 @@ EXL3B_OK = 0
 EXL3B_DECLINED = 1
 EXL3B_BAD_ARG = 2
 EXL3B_WORKSPACE = 3
+EXL3B_TOO_LARGE = 4
 
 c_u16p = ctypes.c_void_p
 c_vp = ctypes.c_void_p
@@ -33,6 +34,7 @@ SIGNATURES = {
                                    ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), i64, c_vp, sz,
                                    c_vp]),
     "exl3b_linear_workspace_error": (i32, [c_vp, ctypes.POINTER(i32), c_vp]),
+    "exl3b_linear_noalloc": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp]),
 }
 
 _lib = None
