@@ -157,9 +157,12 @@ def run_layer(torch, layer, x, inputs, K, tp, pg):
 
 
 def layer_bytes(K, m, tp):
-    """Algorithmic bytes of one layer summed over all tp shards."""
+    """Algorithmic bytes of the step's modules summed over all tp shards."""
     total = 0
+    names = {nm for _, nms in MODULES for nm in nms}
     for name, k, n, rowp in LAYER:
+        if name not in names:
+            continue
         for r in range(tp):
             ks, ns = shard_shape(k, n, rowp, tp, r)
             total += linear_bytes(ks, ns, K, m)
@@ -182,7 +185,7 @@ def _cpu_slice(args):
     return time.perf_counter() - t0
 
 
-def cpu_baseline(K: int, budget_cols: int = 8704) -> dict:
+def cpu_baseline(K: int, budget_cols: int = 17408) -> dict:
     """Time the oracle's linear (M=1, mul1) on a column sample of the gate layer, one slice per
     host core in a spawn pool; report the metric's unit for that sample."""
     import multiprocessing as mp
@@ -214,6 +217,8 @@ def main():
     ap.add_argument("--bits", type=int, default=4)
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--modules", default="qkv,o,gate_up,down",
+                    help="comma list of the layer's modules a step runs (default: all four)")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
 
@@ -221,8 +226,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     K, M = args.bits, args.m
+    global MODULES
+    wanted = args.modules.split(",")
+    MODULES = [mod for mod in MODULES if mod[0] in wanted]
+    assert MODULES, f"no known module in {args.modules}"
 
-    config = {"workload": f"one 27B-class decoder layer's EXL3 linears (qkv, o, gate_up, down), M={M}, "
+    config = {"workload": f"one 27B-class decoder layer's EXL3 linears ({','.join(m_ for m_, _ in MODULES)}), M={M}, "
                           f"{K} bits, mul1 codebook, x bf16 cast to fp16", "model": "synthetic 27B-class layer",
               "hidden": HIDDEN, "intermediate": INTER, "m": M, "bits": K, "tp": world,
               "parallelism": f"tp{world}" if world > 1 else "single", "l2": "weights rotate over copies > 2x L2"}

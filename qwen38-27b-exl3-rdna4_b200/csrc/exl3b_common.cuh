@@ -213,11 +213,13 @@ EXL3B_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }\n"
                  :: "r"(bar), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting warp sleeps in hardware (up to ~20 us per try)
+// instead of spinning through issue slots that the decoding warps need
 EXL3B_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }\n"
-        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }\n"
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(20000u) : "memory");
     return ok != 0;
 }
 
