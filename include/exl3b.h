@@ -104,6 +104,69 @@ EXL3B_API int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, 
                          const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Paged KV cache, head size 128.  Caches are [num_blocks][block_size][num_kv_heads][row] with
+ * row = 128 int8 (int8) or 64 bytes of nibbles (int4: element 2i in the low nibble of byte i),
+ * and per-(token, head) fp32 scales [num_blocks][block_size][num_kv_heads] (int4: the zero point
+ * is stored in the scale's low 4 mantissa bits).  key/value inputs are [tokens][heads][128] with
+ * the given strides (elements), dtype 0 = fp16, 1 = bf16.  slot_mapping[t] = block * block_size +
+ * offset, negative = skip.
+ * ------------------------------------------------------------------------------------------ */
+
+/* int8 per-token-head quantize-on-write: scale = max(absmax/127, 1e-6), q = trunc(clamp(x/scale)).
+ * Replaces vLLM's triton_reshape_and_cache_flash_per_token_head_quant, which the reference's
+ * int8_per_token_head cache uses (vllm/v1/attention/ops/triton_reshape_and_cache_flash.py:139-238). */
+EXL3B_API int exl3b_kv_int8_write(const void* key, const void* value, int dtype, int64_t num_tokens,
+                                  int num_kv_heads, int head_size, int64_t k_stride_tok, int64_t k_stride_head,
+                                  int64_t v_stride_tok, int64_t v_stride_head, int8_t* key_cache,
+                                  int8_t* value_cache, float* k_scale, float* v_scale, const int64_t* slot_mapping,
+                                  int block_size, void* stream);
+
+/* int4 quantize-on-write: y = H (x * signs) unnormalised (+ optional rotated-domain bias [heads][128]),
+ * 3x3 clip search, asymmetric 4 bit, nibble packing.  With exact_tag != NULL also keeps exact fp16 y
+ * rows per request slot: [slots][4 + 128][heads][128] for K (exact_k) and V (exact_v), tags
+ * [slots][4 + 128]; position p < 4 -> row p, else row 4 + p % 128, written when p < 4 or p is among
+ * the sequence's newest 128 positions.  query_start_loc [num_seqs + 1], seq_lens [num_seqs] (length
+ * after this write) and seq_slots [num_seqs] (request slot, < 0 = none) locate each token.
+ * Replaces the reference's kv_int4.reshape_and_cache (vllm_plugin/exl3rocm/kv_int4.py:176-213). */
+EXL3B_API int exl3b_kv_int4_write(const void* key, const void* value, int dtype, int64_t num_tokens,
+                                  int num_kv_heads, int head_size, int64_t k_stride_tok, int64_t k_stride_head,
+                                  int64_t v_stride_tok, int64_t v_stride_head, uint8_t* key_cache,
+                                  uint8_t* value_cache, float* k_scale, float* v_scale, const int64_t* slot_mapping,
+                                  int block_size, const float* rht_signs, const float* bias_k, const float* bias_v,
+                                  const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* seq_slots,
+                                  int num_seqs, uint16_t* exact_k, uint16_t* exact_v, int32_t* exact_tag,
+                                  void* stream);
+
+/* Workspace of the attention calls (split-KV partials; int4 also its rotated q). */
+EXL3B_API size_t exl3b_kv_attn_workspace_bytes(int num_tokens, int num_q_heads, int num_seqs, int num_kv_heads,
+                                               int max_seq_len);
+
+/* Causal decode / speculative-verify attention over the int8 cache: q [tokens][q_heads][128] fp16,
+ * out likewise; query token i of a sequence with q_len = qsl[s+1] - qsl[s] tokens sits at position
+ * seq_lens[s] - q_len + i.  max_q_len * (q_heads / kv_heads) <= 32.  block_table [num_seqs][bt_stride]
+ * int32, block_size a power of two.  Split-KV with a reduce, as vLLM's 3D unified attention with
+ * per-token-head scales (vllm/v1/attention/ops/triton_unified_attention.py:473-545, 646-762). */
+EXL3B_API int exl3b_kv_int8_attn(const uint16_t* q, uint16_t* out, int num_tokens, int num_q_heads,
+                                 int num_kv_heads, int head_size, const int8_t* key_cache, const int8_t* value_cache,
+                                 const float* k_scale, const float* v_scale, int block_size,
+                                 const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                                 const int32_t* query_start_loc, int num_seqs, int max_q_len, int max_seq_len,
+                                 float softmax_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same over the int4 cache: q is rotated with the RHT, rows with a matching exact tag (first 4
+ * and newest 128 positions of a request slot) are read from the exact fp16 rows, and the output is
+ * rotated back: out = H(rot) * signs / 128.  Replaces the reference's kv_int4.attention
+ * (vllm_plugin/exl3rocm/kv_int4.py:345-563). */
+EXL3B_API int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_tokens, int num_q_heads,
+                                 int num_kv_heads, int head_size, const uint8_t* key_cache,
+                                 const uint8_t* value_cache, const float* k_scale, const float* v_scale,
+                                 int block_size, const int32_t* block_table, int64_t bt_stride,
+                                 const int32_t* seq_lens, const int32_t* query_start_loc, int num_seqs,
+                                 int max_q_len, int max_seq_len, float softmax_scale, const float* rht_signs,
+                                 const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
+                                 const int32_t* seq_slots, void* workspace, size_t workspace_bytes, void* stream);
+
 /* exl3b_linear without a caller-provided workspace, for callers that cannot allocate device
  * memory: code that runs while a CUDA graph is being captured (cudaMalloc is not allowed there),
  * hosts whose device memory is owned by a pool the caller cannot reach, and latency-critical

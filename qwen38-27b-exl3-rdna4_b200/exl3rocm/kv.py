@@ -1,0 +1,225 @@
+"""Paged KV cache (int8 and int4 per-token-head) on libexl3b, drop-in for the reference's
+``vllm_plugin/exl3rocm/kv_int4.py`` surface and for vLLM's int8 per-token-head write/attention the
+reference runs for ``int8_per_token_head``.
+
+* int4: ``reshape_and_cache`` (kv_int4.py:176-213) rotates, quantises and packs K/V rows and keeps
+  exact fp16 rows for each request's first 4 and newest 128 positions; ``attention`` (:516-563)
+  runs split-KV decode / verify attention with exact-row substitution and un-rotates the output.
+  Request slots follow kv_int4.py:63-89 (``configure_request_slots``, ``request_added``,
+  ``set_batch_slots``).  The exact rows are kept per request slot (the reference keeps the sinks
+  per physical block; for the sequences' first positions the two agree).
+* int8: ``reshape_and_cache_int8`` and ``attention_int8`` take the arguments of vLLM's
+  per-token-head write and unified attention.
+
+The RHT sign vector is a fixed seeded +-1 vector (``rht_signs``); writes and reads share it, so the
+cache is self-consistent.  There is no CPU path: every call runs on the CUDA library.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import torch
+
+from . import _lib
+
+HEAD_SIZE = 128
+SINKS = int(os.environ.get("EXL3_KV_INT4_SINKS", "4"))
+TAIL = int(os.environ.get("EXL3_KV_INT4_TAIL", "128"))
+MAX_ROWS = 32  # query rows (query tokens x GQA heads) one attention call takes per sequence
+RHT_SEED = 0x5EED1234
+
+_signs: dict = {}
+_exact: dict = {}
+_ws: dict = {}
+_req = {"slot": None, "rows": 0}
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _capturing() -> bool:
+    return torch.cuda.is_current_stream_capturing()
+
+
+def rht_signs(device, d: int = HEAD_SIZE) -> torch.Tensor:
+    """The RHT's +-1 vector (fp32 on the device; built on the CPU once, outside graph capture)."""
+    key = (d, str(device))
+    if key not in _signs:
+        bits = np.random.default_rng(RHT_SEED).integers(0, 2, size=d)
+        _signs[key] = torch.from_numpy(np.where(bits == 1, 1.0, -1.0).astype(np.float32)).to(device)
+    return _signs[key]
+
+
+# ---------------------------------------------------------------------------------------------
+# request slots and exact rows (kv_int4.py:63-118)
+# ---------------------------------------------------------------------------------------------
+def configure_request_slots(max_reqs: int) -> None:
+    """The model runner keeps per-request state in max_reqs fixed slots; slot max_reqs is scratch."""
+    _req["rows"] = max_reqs + 1
+
+
+def _slot_buffer(device):
+    if _req["slot"] is None and _req["rows"] > 0:
+        _req["slot"] = torch.full((1024,), _req["rows"] - 1, dtype=torch.int32, device=device)
+    return _req["slot"]
+
+
+def set_batch_slots(idx_mapping: torch.Tensor) -> None:
+    """batch row -> request slot, in the persistent buffer the captured kernels read."""
+    buf = _slot_buffer(idx_mapping.device)
+    if buf is None:
+        return
+    n = idx_mapping.shape[0]
+    buf[:n].copy_(idx_mapping)
+    buf[n:].fill_(_req["rows"] - 1)
+
+
+def request_added(idx: int) -> None:
+    """A new request took slot idx: forget the previous request's exact rows (tags are positions)."""
+    for b in _exact.values():
+        b["tag"][idx].fill_(-1)
+
+
+def exact_buffers(name, heads: int, device, d: int = HEAD_SIZE):
+    """Exact fp16 rows of layer `name`: [slots, SINKS + TAIL, heads, d] for K and V plus int32 tags
+    [slots, SINKS + TAIL] (-1 = empty).  Allocated on first eager use; None without request slots,
+    with SINKS = TAIL = 0, or when first seen during graph capture."""
+    if not name or _req["rows"] <= 0 or (SINKS <= 0 and TAIL <= 0):
+        return None
+    if name not in _exact:
+        if _capturing():
+            return None
+        rows = _req["rows"]
+        _exact[name] = {
+            "k": torch.zeros((rows, SINKS + TAIL, heads, d), dtype=torch.float16, device=device),
+            "v": torch.zeros((rows, SINKS + TAIL, heads, d), dtype=torch.float16, device=device),
+            "tag": torch.full((rows, SINKS + TAIL), -1, dtype=torch.int32, device=device)}
+    return _exact[name]
+
+
+def _workspace(device, nbytes: int) -> torch.Tensor:
+    key = (torch.device(device).index, _stream(device))
+    ws = _ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if _capturing():
+            raise RuntimeError("exl3rocm.kv: attention workspace too small during graph capture; "
+                               "call reserve_attention_workspace() before capturing")
+        _ws[key] = ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+    return ws
+
+
+def reserve_attention_workspace(device, num_tokens: int, num_q_heads: int, num_seqs: int, num_kv_heads: int,
+                                max_seq_len: int) -> None:
+    _workspace(device, int(_lib.lib().exl3b_kv_attn_workspace_bytes(num_tokens, num_q_heads, num_seqs,
+                                                                     num_kv_heads, max_seq_len)))
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float16:
+        return 0
+    if t.dtype == torch.bfloat16:
+        return 1
+    raise TypeError(f"exl3rocm.kv: key/value must be fp16 or bf16, got {t.dtype}")
+
+
+def _check_rows(t: torch.Tensor, name: str):
+    assert t.dim() == 3 and t.shape[-1] == HEAD_SIZE and t.stride(-1) == 1, f"{name}: [tokens, heads, 128]"
+
+
+# ---------------------------------------------------------------------------------------------
+# writes
+# ---------------------------------------------------------------------------------------------
+def reshape_and_cache_int8(key, value, key_cache, value_cache, slot_mapping, k_scale_cache, v_scale_cache):
+    """vLLM int8_per_token_head write (triton_reshape_and_cache_flash.py:139-238)."""
+    _check_rows(key, "key")
+    _check_rows(value, "value")
+    n = min(key.shape[0], slot_mapping.shape[0])
+    if n == 0:
+        return
+    assert key_cache.is_contiguous() and value_cache.is_contiguous() and k_scale_cache.is_contiguous()
+    slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+    _lib.call("exl3b_kv_int8_write", key.data_ptr(), value.data_ptr(), _dtype_code(key), n, key.shape[1],
+              HEAD_SIZE, key.stride(0), key.stride(1), value.stride(0), value.stride(1), key_cache.data_ptr(),
+              value_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(), slots.data_ptr(),
+              key_cache.shape[1], _stream(key.device))
+
+
+def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, *, k_scale_cache, v_scale_cache,
+                      layer_name=None, query_start_loc=None, seq_lens=None):
+    """int4 write (kv_int4.py:176-213): rotate, clip-search quantise, pack; exact rows when the layer
+    has them and the batch metadata (query_start_loc, seq_lens) is given."""
+    _check_rows(key, "key")
+    _check_rows(value, "value")
+    n = min(key.shape[0], slot_mapping.shape[0])
+    if n == 0:
+        return
+    heads = key.shape[1]
+    slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+    ex = exact_buffers(layer_name, heads, key.device) if query_start_loc is not None else None
+    num_seqs = int(seq_lens.shape[0]) if (ex is not None and seq_lens is not None) else 0
+    use_ex = ex is not None and num_seqs > 0
+    qsl = query_start_loc.to(torch.int32) if use_ex and query_start_loc.dtype != torch.int32 else query_start_loc
+    sl = seq_lens.to(torch.int32) if use_ex and seq_lens.dtype != torch.int32 else seq_lens
+    _lib.call("exl3b_kv_int4_write", key.data_ptr(), value.data_ptr(), _dtype_code(key), n, heads, HEAD_SIZE,
+              key.stride(0), key.stride(1), value.stride(0), value.stride(1), key_cache.data_ptr(),
+              value_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(), slots.data_ptr(),
+              key_cache.shape[1], rht_signs(key.device).data_ptr(), None, None,
+              qsl.data_ptr() if use_ex else None, sl.data_ptr() if use_ex else None,
+              _req["slot"].data_ptr() if use_ex else None, num_seqs,
+              ex["k"].data_ptr() if use_ex else None, ex["v"].data_ptr() if use_ex else None,
+              ex["tag"].data_ptr() if use_ex else None, _stream(key.device))
+
+
+# ---------------------------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------------------------
+def supported(kw) -> bool:
+    """Features the kernels leave out (kv_int4.py:499-504): the caller falls back otherwise."""
+    q = kw["q"]
+    return (kw.get("alibi_slopes") is None and kw.get("sinks") is None and not kw.get("softcap")
+            and kw.get("qq_bias") is None and kw.get("mm_prefix_range") is None and kw.get("output_scale") is None
+            and tuple(kw.get("window_size", (-1, -1)))[0] < 0 and kw.get("causal", True) is True
+            and q.dtype == torch.float16 and q.shape[-1] == HEAD_SIZE
+            and int(kw.get("max_seqlen_q", 1)) * (q.shape[1] // kw["k"].shape[2]) <= MAX_ROWS)
+
+
+def _attn(kind, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale,
+          k_scale_cache, v_scale_cache, max_seqlen_k, layer_name):
+    T, hq, d = q.shape
+    hkv = k.shape[2]
+    assert d == HEAD_SIZE and q.is_contiguous() and out.is_contiguous() and q.dtype == torch.float16
+    num_seqs = seqused_k.shape[0]
+    max_k = int(max_seqlen_k) if max_seqlen_k is not None else int(block_table.shape[1] * k.shape[1])
+    nbytes = int(_lib.lib().exl3b_kv_attn_workspace_bytes(T, hq, num_seqs, hkv, max_k))
+    ws = _workspace(q.device, nbytes)
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    sl = seqused_k if seqused_k.dtype == torch.int32 else seqused_k.to(torch.int32)
+    qsl = cu_seqlens_q if cu_seqlens_q.dtype == torch.int32 else cu_seqlens_q.to(torch.int32)
+    common = (q.data_ptr(), out.data_ptr(), T, hq, hkv, d, k.data_ptr(), v.data_ptr(), k_scale_cache.data_ptr(),
+              v_scale_cache.data_ptr(), k.shape[1], bt.data_ptr(), bt.stride(0), sl.data_ptr(), qsl.data_ptr(),
+              num_seqs, int(max_seqlen_q), max_k, float(softmax_scale))
+    if kind == 8:
+        _lib.call("exl3b_kv_int8_attn", *common, ws.data_ptr(), ws.numel(), _stream(q.device))
+        return
+    ex = _exact.get(layer_name) if layer_name else None
+    use_ex = ex is not None and _req["slot"] is not None
+    _lib.call("exl3b_kv_int4_attn", *common, rht_signs(q.device).data_ptr(),
+              ex["k"].data_ptr() if use_ex else None, ex["v"].data_ptr() if use_ex else None,
+              ex["tag"].data_ptr() if use_ex else None, _req["slot"].data_ptr() if use_ex else None,
+              ws.data_ptr(), ws.numel(), _stream(q.device))
+
+
+def attention(*, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale,
+              k_scale_cache, v_scale_cache, max_seqlen_k=None, layer_name=None, **_):
+    """int4 paged decode / verify attention (kv_int4.py:516-563); writes the un-rotated result to out."""
+    _attn(4, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale, k_scale_cache,
+          v_scale_cache, max_seqlen_k, layer_name)
+
+
+def attention_int8(*, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale,
+                   k_scale_cache, v_scale_cache, max_seqlen_k=None, **_):
+    """int8 per-token-head paged decode / verify attention (vLLM unified attention, 3D split)."""
+    _attn(8, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale, k_scale_cache,
+          v_scale_cache, max_seqlen_k, None)
