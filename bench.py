@@ -206,6 +206,109 @@ def cpu_baseline(K: int, budget_cols: int = 17408) -> dict:
 
 
 # ---------------------------------------------------------------------------------------------
+# paged KV attention and prefill (M = 2048)
+# ---------------------------------------------------------------------------------------------
+KV_HQ, KV_HKV, KV_D, KV_BS = 40, 8, 128, 16
+
+
+def _flush_l2(torch, buf):
+    buf.add_(1)  # a write larger than L2 between timed calls
+
+
+def bench_kv(torch, dev, kind: int, ctx: int, batch: int, q_len: int, iters: int = 5) -> dict:
+    """Decode (q_len 1) or verify attention over an int8 / int4 cache of `batch` sequences of `ctx`
+    tokens, 40 q heads / 8 kv heads, head 128, block 16.  K/V are written through the write kernel
+    from N(0,1) rows with 1 % of channels x8.  GB/s counts the cache bytes the call must read."""
+    from exl3rocm import kv as xkv
+    nblk = batch * ((ctx + KV_BS - 1) // KV_BS)
+    row_bytes = KV_D if kind == 8 else KV_D // 2
+    kc = torch.empty((nblk, KV_BS, KV_HKV, row_bytes), dtype=torch.int8 if kind == 8 else torch.uint8, device=dev)
+    vc = torch.empty_like(kc)
+    ks = torch.empty((nblk, KV_BS, KV_HKV), dtype=torch.float32, device=dev)
+    vs = torch.empty_like(ks)
+    g = torch.Generator(device=dev)
+    g.manual_seed(31 + ctx + batch)
+    bt = torch.randperm(nblk, generator=g, device=dev).to(torch.int32).view(batch, -1)
+    ch = torch.randperm(KV_D, generator=g, device=dev)[: max(1, KV_D // 100)]
+    if kind == 4:
+        xkv.configure_request_slots(batch)
+        xkv._req["slot"] = None
+        xkv._exact.pop("bench", None)
+        xkv.set_batch_slots(torch.arange(batch, dtype=torch.int32, device=dev))
+    chunk = 8192
+    for s in range(batch):
+        if kind == 4:
+            xkv.set_batch_slots(torch.tensor([s], dtype=torch.int32, device=dev))  # this sequence's slot
+        for t0 in range(0, ctx, chunk):
+            n = min(chunk, ctx - t0)
+            k = torch.randn((n, KV_HKV, KV_D), generator=g, device=dev)
+            v = torch.randn((n, KV_HKV, KV_D), generator=g, device=dev)
+            k[..., ch] *= 8
+            v[..., ch] *= 8
+            pos = torch.arange(t0, t0 + n, device=dev)
+            slots = (bt[s, pos // KV_BS].to(torch.int64) * KV_BS + pos % KV_BS)
+            if kind == 8:
+                xkv.reshape_and_cache_int8(k.half(), v.half(), kc, vc, slots, ks, vs)
+            else:
+                xkv.reshape_and_cache(k.half(), v.half(), kc, vc, slots, k_scale_cache=ks, v_scale_cache=vs,
+                                      layer_name="bench",
+                                      query_start_loc=torch.tensor([0, n], dtype=torch.int32, device=dev),
+                                      seq_lens=torch.tensor([t0 + n], dtype=torch.int32, device=dev))
+    if kind == 4:
+        xkv.set_batch_slots(torch.arange(batch, dtype=torch.int32, device=dev))
+    T = batch * q_len
+    q = torch.randn((T, KV_HQ, KV_D), generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    qsl = torch.arange(0, T + 1, q_len, dtype=torch.int32, device=dev)
+    sl = torch.full((batch,), ctx, dtype=torch.int32, device=dev)
+    fn = xkv.attention_int8 if kind == 8 else xkv.attention
+    args = dict(q=q, k=kc, v=vc, out=out, cu_seqlens_q=qsl, max_seqlen_q=q_len, seqused_k=sl, block_table=bt,
+                softmax_scale=KV_D ** -0.5, k_scale_cache=ks, v_scale_cache=vs, max_seqlen_k=ctx, layer_name="bench")
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > L2
+    fn(**args)
+    times = []
+    for _ in range(iters):
+        _flush_l2(torch, flush)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn(**args)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    kv_bytes = batch * ctx * KV_HKV * (2 * row_bytes + 8)
+    del kc, vc, ks, vs, flush
+    return {"cache": f"int{kind}", "ctx": ctx, "batch": batch, "q_len": q_len, "ms": ms,
+            "gb_s": kv_bytes / (ms * 1e-3) / 1e9, "kv_bytes": kv_bytes}
+
+
+def bench_prefill(torch, dev, K: int, m: int = 2048, iters: int = 5) -> dict:
+    """One gate_up-shaped EXL3 linear (5120 -> 17408) at M rows through the public op."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    tr = torch.randint(-32768, 32768, (HIDDEN // 16, INTER // 16, 16 * K), generator=g, device=dev,
+                       dtype=torch.int32).to(torch.int16)
+    suh = (torch.randint(0, 2, (HIDDEN,), generator=g, device=dev) * 2 - 1).half()
+    svh = (torch.randint(0, 2, (INTER,), generator=g, device=dev) * 2 - 1).half()
+    x = torch.randn((m, HIDDEN), generator=g, device=dev).to(torch.bfloat16)
+    from exl3rocm import ops as xops
+    xops.reserve_weight_buffer(dev, HIDDEN * INTER)
+    torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, True)
+    times = []
+    for _ in range(iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, True)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    return {"m": m, "k": HIDDEN, "n": INTER, "bits": K, "ms": ms,
+            "tflops": 2.0 * m * HIDDEN * INTER / (ms * 1e-3) / 1e12,
+            "route": "had128 + dequant to fp16 + dense fp16 GEMM (torch.mm) + had128"}
+
+
+# ---------------------------------------------------------------------------------------------
 # main
 # ---------------------------------------------------------------------------------------------
 def main():
@@ -217,6 +320,7 @@ def main():
     ap.add_argument("--bits", type=int, default=4)
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extra", action="store_true", help="skip the KV-attention and prefill legs")
     ap.add_argument("--modules", default="qkv,o,gate_up,down",
                     help="comma list of the layer's modules a step runs (default: all four)")
     args = ap.parse_args()
@@ -382,6 +486,13 @@ def main():
     e2e_value = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
     del graphs, gu_graphs
 
+    extra = {}
+    if world == 1 and not args.no_extra:
+        extra["kv_attention"] = [bench_kv(torch, dev, kind, ctx, b, ql)
+                                 for kind, ctx, b, ql in ((8, 32768, 8, 1), (4, 32768, 8, 1), (8, 32768, 1, 4),
+                                                          (4, 65536, 1, 1), (8, 4096, 8, 1))]
+        extra["prefill_m2048"] = bench_prefill(torch, dev, K)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(K)
@@ -407,6 +518,7 @@ def main():
                 "d2h_bytes_per_step": int(y_host.numel() * 2)},
         "gpu_launches": args.steps * 2 * len(MODULES),
         "clocks": clocks,
+        **extra,
     }
     print(json.dumps(line))
 

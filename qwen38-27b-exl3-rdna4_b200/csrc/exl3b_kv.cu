@@ -292,9 +292,35 @@ struct KvTraits<4> {
     EXL3B_DEV static int jB(int p) { return 8 * (p / 4) + p % 4 + 4; }
 };
 
+// Per-warp shared memory: a ring of kRing tiles (32 tokens: K rows, V rows, k scales, v scales)
+// filled with cp.async one tile ahead of the math, and a window of the split's block ids.
+template <int KV>
+struct AttnSmem {
+    static constexpr int kRowBytes = KV == 8 ? kHD : kHD / 2;
+    static constexpr int kRows = 32 * kRowBytes;                  // K (or V) bytes of one tile
+    static constexpr int kTile = 2 * kRows + 2 * 32 * 4;          // K, V, k scales, v scales
+    static constexpr int kRing = KV == 8 ? 2 : 3;
+    static constexpr int kBtWindow = 256;                          // block ids kept per warp
+    static constexpr int kWarpBytes = kRing * kTile + kBtWindow * 4;
+};
+
+EXL3B_DEV void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" :: "r"(dst), "l"(src) : "memory");
+}
+EXL3B_DEV void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" :: "r"(dst), "l"(src) : "memory");
+}
+EXL3B_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+EXL3B_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
+
 template <int KV, int MT>
 __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
     using Tr = KvTraits<KV>;
+    using SM = AttnSmem<KV>;
+    constexpr int RB = SM::kRowBytes;
+    constexpr int C16 = RB / 16;  // 16-byte chunks per row (8 or 4)
+    extern __shared__ __align__(128) uint8_t smem_raw[];
     const int seq = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
@@ -308,8 +334,15 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
     if (t_lo >= t_hi) return;  // empty split: the reduce kernel skips it
     // row r of the sequence = query (r / G), head kvh*G + r % G; this warp owns rows 16w .. 16w+15
     const int rbase = 16 * warp;
-    if (rbase >= rows) return;
+    if (rbase >= rows) return;  // no CTA-wide barrier below: warps run independently
     const int r_lo = rbase + gq, r_hi = rbase + gq + 8;
+
+    uint8_t* wsm = smem_raw + warp * SM::kWarpBytes;
+    const uint32_t wsm_u = smem_u32(wsm);
+    int32_t* bt_win = reinterpret_cast<int32_t*>(wsm + SM::kRing * SM::kTile);
+    const int32_t* bt = a.block_table + (int64_t)seq * a.bt_stride;
+    const int lg = a.block_size_log2, bs_mask = (1 << lg) - 1;
+    int win_base = -1;  // first block index held in bt_win
 
     // ---- Q fragments: A[r][k-slot] = Q[row r][dmap] ----
     uint32_t qa[8][4];
@@ -329,6 +362,47 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
         }
     }
 
+    // ---- tile loader: all of a 32-token tile's rows and scales, one cp.async group ----
+    // Row r of a tile is stored with its 16-byte chunks XOR-swizzled by (r & (C16 - 1)), so that
+    // the lanes reading the same chunk index of different rows hit different banks.
+    const int ntiles = (t_hi - t_lo + 31) >> 5;
+    auto issue_tile = [&](int ti) {
+        const int t0 = t_lo + 32 * ti;
+        // block-id window: refill when the tile leaves it (the window is private to this warp)
+        const int b_first = t0 >> lg, b_last = min(t0 + 31, t_hi - 1) >> lg;
+        if (win_base < 0 || b_first < win_base || b_last >= win_base + SM::kBtWindow) {
+            __syncwarp();
+            win_base = b_first;
+            const int nb = min(SM::kBtWindow, ((t_hi - 1) >> lg) - b_first + 1);
+            for (int i = lane; i < nb; i += 32) bt_win[i] = bt[b_first + i];
+            __syncwarp();
+        }
+        const uint32_t tb = wsm_u + (ti % SM::kRing) * SM::kTile;
+#pragma unroll
+        for (int j = 0; j < C16; ++j) {  // 32 rows x C16 chunks, C16 per lane per side
+            const int cidx = lane + 32 * j;
+            const int r = cidx / C16, ch = cidx % C16;
+            const int t = t0 + r;
+            if (t < t_hi) {
+                const int64_t blk = bt_win[(t >> lg) - win_base];
+                const int64_t row = ((blk << lg) + (t & bs_mask)) * a.num_kv_heads + kvh;
+                const uint32_t soff = r * RB + ((ch ^ (r & (C16 - 1))) * 16);
+                cp_async16(tb + soff, reinterpret_cast<const uint8_t*>(a.key_cache) + row * RB + ch * 16);
+                cp_async16(tb + SM::kRows + soff, reinterpret_cast<const uint8_t*>(a.value_cache) + row * RB + ch * 16);
+            }
+        }
+        {
+            const int t = t0 + lane;
+            if (t < t_hi) {
+                const int64_t blk = bt_win[(t >> lg) - win_base];
+                const int64_t row = ((blk << lg) + (t & bs_mask)) * a.num_kv_heads + kvh;
+                cp_async4(tb + 2 * SM::kRows + lane * 4, a.k_scale + row);
+                cp_async4(tb + 2 * SM::kRows + 128 + lane * 4, a.v_scale + row);
+            }
+        }
+        cp_async_commit();
+    };
+
     float m_i[2] = {-INFINITY, -INFINITY}, l_i[2] = {0.f, 0.f};
     float acc[16][4];
 #pragma unroll
@@ -338,14 +412,7 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
     // causal limit of rows g and g+8: key t allowed if t <= L - qlen + query index
     const int lim0 = (r_lo < rows) ? L - qlen + r_lo / G : -1;
     const int lim1 = (r_hi < rows) ? L - qlen + r_hi / G : -1;
-
-    const int32_t* bt = a.block_table + (int64_t)seq * a.bt_stride;
-    const int bs_mask = (1 << a.block_size_log2) - 1;
     const int rs = (KV == 4 && a.seq_slots) ? a.seq_slots[seq] : -1;
-    auto row_index = [&](int t) -> int64_t {
-        const int64_t blk = bt[t >> a.block_size_log2];
-        return ((blk << a.block_size_log2) + (t & bs_mask)) * a.num_kv_heads + kvh;
-    };
     auto exact_of = [&](int t) -> int {  // exact row of position t, or -1 (int4 only)
         if (KV != 4 || rs < 0 || a.exact_tag == nullptr) return -1;
         if (!(t < kSinks || t >= L - kTail)) return -1;
@@ -353,19 +420,32 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
         return a.exact_tag[(int64_t)rs * kExactRows + e] == t ? e : -1;
     };
 
-    for (int t0 = t_lo; t0 < t_hi; t0 += 32) {
+    for (int ti = 0; ti < SM::kRing - 1 && ti < ntiles; ++ti) issue_tile(ti);
+
+    for (int ti = 0; ti < ntiles; ++ti) {
+        if (ti + SM::kRing - 1 < ntiles) issue_tile(ti + SM::kRing - 1);
+        else cp_async_commit();  // keep the group count in step
+        cp_async_wait<SM::kRing - 1>();
+        __syncwarp();
+        const int t0 = t_lo + 32 * ti;
+        const uint8_t* tile = wsm + (ti % SM::kRing) * SM::kTile;
+        const float* ksc_s = reinterpret_cast<const float*>(tile + 2 * SM::kRows);
+        const float* vsc_s = ksc_s + 32;
+        auto chunk_at = [&](int side, int r, int ch) -> uint4 {
+            return *reinterpret_cast<const uint4*>(tile + side * SM::kRows + r * RB + ((ch ^ (r & (C16 - 1))) * 16));
+        };
+
         // ---------------- S = Q K^T for 4 n-tiles of 8 tokens ----------------
         float s[4][4];
-        float ksc_tok[4];  // scale of token 8n + gq, the token this lane feeds as the B operand
+        float ksc_tok[4];
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
-            const int t = t0 + 8 * n + gq;
+            const int r = 8 * n + gq, t = t0 + r;
             uint32_t b[8][2];
             float ksc = 0.f;
 #pragma unroll
             for (int c = 0; c < 8; ++c) b[c][0] = b[c][1] = 0u;
             if (t < t_hi) {
-                const int64_t row = row_index(t);
                 const int e = exact_of(t);
                 if (e >= 0) {
                     const __half* ex = a.exact_k + (((int64_t)rs * kExactRows + e) * a.num_kv_heads + kvh) * kHD;
@@ -376,18 +456,15 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
                     }
                     ksc = 1.f;
                 } else if constexpr (KV == 8) {
-                    const uint4* kp = reinterpret_cast<const uint4*>(
-                        reinterpret_cast<const int8_t*>(a.key_cache) + row * kHD + 32 * tq);
-                    const uint4 w0 = __ldg(kp), w1 = __ldg(kp + 1);
+                    const uint4 w0 = chunk_at(0, r, 2 * tq), w1 = chunk_at(0, r, 2 * tq + 1);
                     const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                     for (int c = 0; c < 8; ++c) i8x4_to_h2(w[c], b[c][0], b[c][1]);
-                    ksc = __ldg(a.k_scale + row);
+                    ksc = ksc_s[r];
                 } else {
-                    const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(
-                        reinterpret_cast<const uint8_t*>(a.key_cache) + row * (kHD / 2) + 16 * tq));
+                    const uint4 w4 = chunk_at(0, r, tq);
                     const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-                    const uint32_t sb = __float_as_uint(__ldg(a.k_scale + row));
+                    const uint32_t sb = __float_as_uint(ksc_s[r]);
                     const uint32_t zp = 0x6400u | (sb & 0xFu);
                     const uint32_t zp2 = zp | (zp << 16);
 #pragma unroll
@@ -451,17 +528,16 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
         // ---------------- O += (P * v_scale) V, two k-chunks of 16 tokens ----------------
 #pragma unroll
         for (int kc = 0; kc < 2; ++kc) {
-            // the lane's four B-operand tokens: 16kc + 2tq + {0, 1, 8, 9}
             float vs4[4];
-            uint32_t vh[4][8];  // half2 pairs (jA(p), jB(p)) of d = 16 gq + j
+            uint32_t vh[4][8];  // half2 pairs (jA(p), jB(p)) of d = 16 gq + j, for the lane's 4 tokens
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int t = t0 + 16 * kc + 2 * tq + (i & 1) + 8 * (i >> 1);
+                const int r = 16 * kc + 2 * tq + (i & 1) + 8 * (i >> 1);
+                const int t = t0 + r;
                 vs4[i] = 0.f;
 #pragma unroll
                 for (int p = 0; p < 8; ++p) vh[i][p] = 0u;
                 if (t < t_hi) {
-                    const int64_t row = row_index(t);
                     const int e = exact_of(t);
                     if (e >= 0) {
                         const uint4* ep = reinterpret_cast<const uint4*>(
@@ -477,19 +553,18 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
                         }
                         vs4[i] = 1.f;
                     } else if constexpr (KV == 8) {
-                        const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(
-                            reinterpret_cast<const int8_t*>(a.value_cache) + row * kHD + 16 * gq));
+                        const uint4 w4 = chunk_at(1, r, gq);
                         const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
                         for (int c = 0; c < 4; ++c) i8x4_to_h2(w[c], vh[i][2 * c], vh[i][2 * c + 1]);
-                        vs4[i] = __ldg(a.v_scale + row);
+                        vs4[i] = vsc_s[r];
                     } else {
-                        const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(
-                            reinterpret_cast<const uint8_t*>(a.value_cache) + row * (kHD / 2) + 8 * gq));
-                        const uint32_t sb = __float_as_uint(__ldg(a.v_scale + row));
+                        // this lane's 8 bytes (d = 16 gq .. 16 gq + 15) are the half gq & 1 of chunk gq / 2
+                        const uint4 w4 = chunk_at(1, r, gq >> 1);
+                        const uint32_t w[2] = {(gq & 1) ? w4.z : w4.x, (gq & 1) ? w4.w : w4.y};
+                        const uint32_t sb = __float_as_uint(vsc_s[r]);
                         const uint32_t zp = 0x6400u | (sb & 0xFu);
                         const uint32_t zp2 = zp | (zp << 16);
-                        const uint32_t w[2] = {w2.x, w2.y};
 #pragma unroll
                         for (int p = 0; p < 8; ++p) vh[i][p] = nib_pair(w[p / 4], p % 4, zp2);
                         vs4[i] = __uint_as_float(sb & 0xFFFFFFF0u);
@@ -512,7 +587,9 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
                 mma_16816(acc[Tr::jB(p)], pa, bB0, bB1);
             }
         }
+        __syncwarp();  // the ring slot of this tile is refilled next iteration
     }
+    cp_async_wait<0>();
 
     // ---- partial of this split: acc (d order restored), m, l ----
     // lane (g, q) holds for row g: d = 32q + j (acc[j][0]) and 32q + 16 + j (acc[j][1]); row g+8: [2], [3]
@@ -537,6 +614,8 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
         }
     }
 }
+
+// ---------------------------------------------------------------------------------------------
 
 // ---------------------------------------------------------------------------------------------
 // split reduce (vLLM reduce_segments), + for int4 the un-rotation out = H(rot) * s / d
@@ -601,6 +680,21 @@ static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len) {
     const int want = (8 * kv_num_sms() + num_seqs * num_kv_heads - 1) / (num_seqs * num_kv_heads);
     const int by_len = (max_seq_len + 63) / 64;
     return std::max(1, std::min(kMaxSplits, std::min(want, by_len)));
+}
+
+template <int KV, int MT>
+static cudaError_t launch_attn(dim3 grid, const KvAttnArgs& a, cudaStream_t st) {
+    const int smem = MT * AttnSmem<KV>::kWarpBytes;
+    static std::once_flag once[64];
+    static cudaError_t attr_err[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(once[dev & 63], [&] {
+        attr_err[dev & 63] = cudaFuncSetAttribute(kv_attn_kernel<KV, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+    if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
+    kv_attn_kernel<KV, MT><<<grid, 32 * MT, smem, st>>>(a);
+    return cudaGetLastError();
 }
 
 static bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
@@ -718,14 +812,9 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     a.exact_tag = exact_tag; a.seq_slots = seq_slots;
     const dim3 grid(num_seqs, num_kv_heads, S);
     const bool two = max_q_len * G > 16;
-    if (kv == 8) {
-        if (two) kv_attn_kernel<8, 2><<<grid, 64, 0, st>>>(a);
-        else kv_attn_kernel<8, 1><<<grid, 32, 0, st>>>(a);
-    } else {
-        if (two) kv_attn_kernel<4, 2><<<grid, 64, 0, st>>>(a);
-        else kv_attn_kernel<4, 1><<<grid, 32, 0, st>>>(a);
-    }
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (kv == 8) e = two ? launch_attn<8, 2>(grid, a, st) : launch_attn<8, 1>(grid, a, st);
+    else e = two ? launch_attn<4, 2>(grid, a, st) : launch_attn<4, 1>(grid, a, st);
     if (e != cudaSuccess) return cuda_status(e);
     KvReduceArgs r = {};
     r.partial = a.partial; r.out = reinterpret_cast<__half*>(out); r.seq_lens = seq_lens;
