@@ -270,17 +270,13 @@ EXL3B_DEV float exp_f(float x) { return exp2f(x * 1.4426950408889634f); }
 template <int KV>
 struct KvTraits;
 
-// The d permutation of the QK^T product, per MMA k-chunk c (0..7) and lane q:
+// The d permutation of the QK^T product, per MMA k-chunk c (0..7) and lane q (= lane & 3):
 //   int8: k-slots (2q, 2q+1, 2q+8, 2q+9) <- d = 32q + 4c + (0, 1, 2, 3)
 //   int4: k-slots (2q, 2q+1, 2q+8, 2q+9) <- d = 32q + 8(c/2) + 2(c%2) + (0, 4, 1, 5)
-// and of P V, per lane g: output column n of n-tile j is d = 16n + j, so lane g reads every token's
-// values at d = 16g .. 16g+15.  In the V half2 pairs p = 0..7 cover (jA(p), jB(p)):
-//   int8: (2p, 2p+1);   int4: (8(p/4) + p%4, 8(p/4) + p%4 + 4)
+// so that one lane's K bytes of a token are contiguous (32 bytes int8, 16 bytes int4).
 template <>
 struct KvTraits<8> {
     EXL3B_DEV static int dmap(int q, int c, int slot) { return 32 * q + 4 * c + slot; }
-    EXL3B_DEV static int jA(int p) { return 2 * p; }
-    EXL3B_DEV static int jB(int p) { return 2 * p + 1; }
 };
 template <>
 struct KvTraits<4> {
@@ -288,8 +284,6 @@ struct KvTraits<4> {
         const int add = (slot == 0) ? 0 : (slot == 1) ? 4 : (slot == 2) ? 1 : 5;
         return 32 * q + 8 * (c / 2) + 2 * (c % 2) + add;
     }
-    EXL3B_DEV static int jA(int p) { return 8 * (p / 4) + p % 4; }
-    EXL3B_DEV static int jB(int p) { return 8 * (p / 4) + p % 4 + 4; }
 };
 
 // Per-warp shared memory: a ring of kRing tiles (32 tokens: K rows, V rows, k scales, v scales)
@@ -314,8 +308,39 @@ EXL3B_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "
 template <int N>
 EXL3B_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
 
-template <int KV, int MT>
-__global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
+// mma.m16n8k16 f16 -> f32 without the volatile qualifier, so that it schedules with the rest
+EXL3B_DEV void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                       uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// 8x8 b16 transpose across the warp: lane l holds row l/4, columns 2(l%4), 2(l%4)+1, before and after
+EXL3B_DEV uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+    return y;
+}
+EXL3B_DEV float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
+}
+EXL3B_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+
+// Attention of one (sequence, KV head, split), transposed: tokens are the MMA's M dimension and
+// query rows its N dimension (8 per n-tile), so that a decode step's GQA group of 5 rows fills 5/8
+// of an n-tile instead of 5/16 of an m-tile.
+//   S^T[token][row] = K[token][:] . Q[row][:]      A = K tile (16 tokens x 16 d), B = Q^T (resident)
+//   O^T[d][row]    += V^T[d][:] . P'^T[:][row]     A = V^T (16 d x 16 tokens), B = P'^T
+// P' = p * v_scale[token] in fp16 leaves the S^T accumulator as (token g, rows 2q, 2q+1) and
+// movmatrix.trans turns each 8x8 block into the B fragment (rows g, tokens 2q, 2q+1).  In PV lane
+// g covers d = 16g .. 16g+15: m-tile j's rows g and g+8 are d = 16g + 2j and 16g + 2j + 1, so a lane
+// reads 16 contiguous bytes (int8) or 8 (int4) of each of its 4 tokens per 16-token chunk.
+// Each warp owns 8 * NT query rows; the CTA's warps share nothing and never wait on one another.
+template <int KV, int NT>
+__global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     using Tr = KvTraits<KV>;
     using SM = AttnSmem<KV>;
     constexpr int RB = SM::kRowBytes;
@@ -323,7 +348,7 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int seq = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gq = lane >> 2, tq = lane & 3;
+    const int g = lane >> 2, q = lane & 3;
     const int L = a.seq_lens[seq];
     const int q0 = a.query_start_loc[seq], qlen = a.query_start_loc[seq + 1] - q0;
     if (qlen <= 0 || L <= 0) return;
@@ -332,10 +357,9 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
     const int per = ((L + a.num_splits - 1) / a.num_splits + 31) & ~31;  // tokens per split, x32
     const int t_lo = split * per, t_hi = min(L, t_lo + per);
     if (t_lo >= t_hi) return;  // empty split: the reduce kernel skips it
-    // row r of the sequence = query (r / G), head kvh*G + r % G; this warp owns rows 16w .. 16w+15
-    const int rbase = 16 * warp;
+    // row r of the sequence = query (r / G), head kvh*G + r % G; this warp owns rows rbase + 0 .. 8NT-1
+    const int rbase = 8 * NT * warp;
     if (rbase >= rows) return;  // no CTA-wide barrier below: warps run independently
-    const int r_lo = rbase + gq, r_hi = rbase + gq + 8;
 
     uint8_t* wsm = smem_raw + warp * SM::kWarpBytes;
     const uint32_t wsm_u = smem_u32(wsm);
@@ -344,21 +368,19 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
     const int lg = a.block_size_log2, bs_mask = (1 << lg) - 1;
     int win_base = -1;  // first block index held in bt_win
 
-    // ---- Q fragments: A[r][k-slot] = Q[row r][dmap] ----
-    uint32_t qa[8][4];
+    // ---- Q^T fragments, resident: B[k-slot][n] = Q[row rbase + 8nt + n][dmap], lane (n = g, slots q) ----
+    uint32_t qb[NT][8][2];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int nt = 0; nt < NT; ++nt) {
+        const int r = rbase + 8 * nt + g;
+        const __half* qrow = a.q + ((int64_t)(q0 + r / G) * a.num_q_heads + kvh * G + r % G) * kHD;
 #pragma unroll
-        for (int hrow = 0; hrow < 2; ++hrow) {
-            const int r = hrow ? r_hi : r_lo;
-            __half v4[4] = {__float2half(0.f), __float2half(0.f), __float2half(0.f), __float2half(0.f)};
-            if (r < rows) {
-                const __half* qrow = a.q + ((int64_t)(q0 + r / G) * a.num_q_heads + kvh * G + r % G) * kHD;
+        for (int c = 0; c < 8; ++c) {
+            __half v4[4];
 #pragma unroll
-                for (int s = 0; s < 4; ++s) v4[s] = qrow[Tr::dmap(tq, c, s)];
-            }
-            qa[c][hrow] = h2_as_u32(__halves2half2(v4[0], v4[1]));      // k-slots 2q, 2q+1
-            qa[c][hrow + 2] = h2_as_u32(__halves2half2(v4[2], v4[3]));  // k-slots 2q+8, 2q+9
+            for (int s = 0; s < 4; ++s) v4[s] = r < rows ? qrow[Tr::dmap(q, c, s)] : __float2half(0.f);
+            qb[nt][c][0] = h2_as_u32(__halves2half2(v4[0], v4[1]));
+            qb[nt][c][1] = h2_as_u32(__halves2half2(v4[2], v4[3]));
         }
     }
 
@@ -403,18 +425,30 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
         cp_async_commit();
     };
 
-    float m_i[2] = {-INFINITY, -INFINITY}, l_i[2] = {0.f, 0.f};
-    float acc[16][4];
+    const float sl2 = a.score_scale * 1.4426950408889634f;  // scores in the log2 domain
+    float m_i[NT][2], l_i[NT][2], lim[NT][2];
+    float acc[NT][8][4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
-    // causal limit of rows g and g+8: key t allowed if t <= L - qlen + query index
-    const int lim0 = (r_lo < rows) ? L - qlen + r_lo / G : -1;
-    const int lim1 = (r_hi < rows) ? L - qlen + r_hi / G : -1;
+        for (int h = 0; h < 2; ++h) {
+            m_i[nt][h] = -INFINITY;
+            l_i[nt][h] = 0.f;
+            // causal limit of row 2q + h: key t allowed if t <= L - qlen + query index
+            const int r = rbase + 8 * nt + 2 * q + h;
+            lim[nt][h] = (r < rows) ? (float)(L - qlen + r / G) : -1.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[nt][j][e] = 0.f;
+    }
+    // the warp's smallest causal limit over its real rows (rows past `rows` are never written)
+    const int lim_lo = L - qlen + rbase / G;
     const int rs = (KV == 4 && a.seq_slots) ? a.seq_slots[seq] : -1;
+    const bool has_exact = KV == 4 && rs >= 0 && a.exact_tag != nullptr;
     auto exact_of = [&](int t) -> int {  // exact row of position t, or -1 (int4 only)
-        if (KV != 4 || rs < 0 || a.exact_tag == nullptr) return -1;
+        if (KV != 4 || !has_exact) return -1;
         if (!(t < kSinks || t >= L - kTail)) return -1;
         const int e = exact_row(t);
         return a.exact_tag[(int64_t)rs * kExactRows + e] == t ? e : -1;
@@ -434,185 +468,284 @@ __global__ void __launch_bounds__(32 * MT) kv_attn_kernel(const KvAttnArgs a) {
         auto chunk_at = [&](int side, int r, int ch) -> uint4 {
             return *reinterpret_cast<const uint4*>(tile + side * SM::kRows + r * RB + ((ch ^ (r & (C16 - 1))) * 16));
         };
+        // this tile holds exact rows only if it meets the first kSinks or the last kTail positions
+        const bool ex_tile = has_exact && (t0 < kSinks || t0 + 31 >= L - kTail);
 
-        // ---------------- S = Q K^T for 4 n-tiles of 8 tokens ----------------
-        float s[4][4];
-        float ksc_tok[4];
+        // K fragments of token r of the tile: k-slot pairs (2q, 2q+1) -> kf[c][0], (2q+8, 2q+9) -> kf[c][1]
+        auto k_frag = [&](int r, uint32_t (&kf)[8][2]) -> float {
+            const int t = t0 + r;
+            if (t >= t_hi) {
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-            const int r = 8 * n + gq, t = t0 + r;
-            uint32_t b[8][2];
-            float ksc = 0.f;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) b[c][0] = b[c][1] = 0u;
-            if (t < t_hi) {
+                for (int c = 0; c < 8; ++c) kf[c][0] = kf[c][1] = 0u;
+                return 0.f;
+            }
+            if (KV == 4 && ex_tile) {
                 const int e = exact_of(t);
                 if (e >= 0) {
                     const __half* ex = a.exact_k + (((int64_t)rs * kExactRows + e) * a.num_kv_heads + kvh) * kHD;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
-                        b[c][0] = h2_as_u32(__halves2half2(ex[Tr::dmap(tq, c, 0)], ex[Tr::dmap(tq, c, 1)]));
-                        b[c][1] = h2_as_u32(__halves2half2(ex[Tr::dmap(tq, c, 2)], ex[Tr::dmap(tq, c, 3)]));
+                        kf[c][0] = h2_as_u32(__halves2half2(ex[Tr::dmap(q, c, 0)], ex[Tr::dmap(q, c, 1)]));
+                        kf[c][1] = h2_as_u32(__halves2half2(ex[Tr::dmap(q, c, 2)], ex[Tr::dmap(q, c, 3)]));
                     }
-                    ksc = 1.f;
-                } else if constexpr (KV == 8) {
-                    const uint4 w0 = chunk_at(0, r, 2 * tq), w1 = chunk_at(0, r, 2 * tq + 1);
-                    const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) i8x4_to_h2(w[c], b[c][0], b[c][1]);
-                    ksc = ksc_s[r];
-                } else {
-                    const uint4 w4 = chunk_at(0, r, tq);
-                    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-                    const uint32_t sb = __float_as_uint(ksc_s[r]);
-                    const uint32_t zp = 0x6400u | (sb & 0xFu);
-                    const uint32_t zp2 = zp | (zp << 16);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        b[c][0] = nib_pair(w[c / 2], 2 * (c % 2), zp2);
-                        b[c][1] = nib_pair(w[c / 2], 2 * (c % 2) + 1, zp2);
-                    }
-                    ksc = __uint_as_float(sb & 0xFFFFFFF0u);
+                    return 1.f;
                 }
             }
-            ksc_tok[n] = ksc;
-            float d4[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (KV == 8) {
+                const uint4 w0 = chunk_at(0, r, 2 * q), w1 = chunk_at(0, r, 2 * q + 1);
+                const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int c = 0; c < 8; ++c) mma_16816(d4, qa[c], b[c][0], b[c][1]);
+                for (int c = 0; c < 8; ++c) i8x4_to_h2(w[c], kf[c][0], kf[c][1]);
+                return ksc_s[r];
+            } else {
+                const uint4 w4 = chunk_at(0, r, q);
+                const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+                const uint32_t sb = __float_as_uint(ksc_s[r]);
+                const uint32_t zp = 0x6400u | (sb & 0xFu);
+                const uint32_t zp2 = zp | (zp << 16);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) s[n][e] = d4[e];
-        }
-        // scale and mask: this lane holds S[row g (e<2) / g+8 (e>=2)][token 8n + 2tq + (e&1)]
-        float mx[2] = {-INFINITY, -INFINITY};
+                for (int c = 0; c < 8; ++c) {
+                    kf[c][0] = nib_pair(w[c / 2], 2 * (c % 2), zp2);
+                    kf[c][1] = nib_pair(w[c / 2], 2 * (c % 2) + 1, zp2);
+                }
+                return __uint_as_float(sb & 0xFFFFFFF0u);
+            }
+        };
+
+        // ---------------- S^T = K Q^T: two m-tiles of 16 tokens ----------------
+        // s[nt][mt][e]: token 16mt + g + 8(e >> 1), row 2q + (e & 1) of n-tile nt
+        float s[NT][2][4];
+        float ksc[2][2];
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
+        for (int mt = 0; mt < 2; ++mt) {
+            uint32_t kA[8][2], kB[8][2];
+            ksc[mt][0] = k_frag(16 * mt + g, kA);
+            ksc[mt][1] = k_frag(16 * mt + g + 8, kB);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int t = t0 + 8 * n + 2 * tq + (e & 1);
-                const float ks = __shfl_sync(0xFFFFFFFFu, ksc_tok[n], (2 * tq + (e & 1)) * 4);
-                const bool ok = t < t_hi && t <= ((e < 2) ? lim0 : lim1);
-                s[n][e] = ok ? s[n][e] * (a.score_scale * ks) : -INFINITY;
-                mx[e >> 1] = fmaxf(mx[e >> 1], s[n][e]);
+            for (int nt = 0; nt < NT; ++nt) {
+                float d4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < 8; ++c) mma_f16(d4, kA[c][0], kB[c][0], kA[c][1], kB[c][1], qb[nt][c][0], qb[nt][c][1]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s[nt][mt][e] = d4[e];
             }
         }
-        float corr[2];
+        // scale (log2 domain) and mask; a tile needs the mask only at the split's end or the causal edge
+        const bool masked = !(t0 + 32 <= t_hi && t0 + 31 <= lim_lo);
+        float mx[NT][2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 1));
-            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 2));
-            const float mnew = fmaxf(m_i[h], mx[h]);
-            corr[h] = (mnew == -INFINITY) ? 1.f : exp_f(m_i[h] - mnew);
-            m_i[h] = mnew;
+        for (int nt = 0; nt < NT; ++nt) {
+            mx[nt][0] = mx[nt][1] = -INFINITY;
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float v = s[nt][mt][e] * (sl2 * ksc[mt][e >> 1]);
+                    if (masked) {
+                        const int t = t0 + 16 * mt + g + 8 * (e >> 1);
+                        v = (t < t_hi && (float)t <= lim[nt][e & 1]) ? v : -INFINITY;
+                    }
+                    s[nt][mt][e] = v;
+                    mx[nt][e & 1] = fmaxf(mx[nt][e & 1], v);
+                }
         }
-        float rowsum[2] = {0.f, 0.f};
+        float corr[NT][2];
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float mm = m_i[e >> 1];
-                const float p = (mm == -INFINITY) ? 0.f : exp_f(s[n][e] - mm);
-                s[n][e] = p;
-                rowsum[e >> 1] += p;
+            for (int h = 0; h < 2; ++h) {
+                float v = mx[nt][h];
+                v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+                v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, 8));
+                v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, 16));
+                const float mnew = fmaxf(m_i[nt][h], v);
+                corr[nt][h] = (mnew == -INFINITY) ? 1.f : ex2(m_i[nt][h] - mnew);
+                m_i[nt][h] = mnew;
             }
+        float rsum[NT][2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            rowsum[h] += __shfl_xor_sync(0xFFFFFFFFu, rowsum[h], 1);
-            rowsum[h] += __shfl_xor_sync(0xFFFFFFFFu, rowsum[h], 2);
-            l_i[h] = l_i[h] * corr[h] + rowsum[h];
+        for (int nt = 0; nt < NT; ++nt) {
+            rsum[nt][0] = rsum[nt][1] = 0.f;
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float mm = m_i[nt][e & 1];
+                    const float p = (mm == -INFINITY) ? 0.f : ex2(s[nt][mt][e] - mm);
+                    s[nt][mt][e] = p;
+                    rsum[nt][e & 1] += p;
+                }
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            acc[j][0] *= corr[0]; acc[j][1] *= corr[0];
-            acc[j][2] *= corr[1]; acc[j][3] *= corr[1];
-        }
-        // ---------------- O += (P * v_scale) V, two k-chunks of 16 tokens ----------------
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v = rsum[nt][h];
+                v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+                v += __shfl_xor_sync(0xFFFFFFFFu, v, 8);
+                v += __shfl_xor_sync(0xFFFFFFFFu, v, 16);
+                l_i[nt][h] = l_i[nt][h] * corr[nt][h] + v;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    acc[nt][j][h] *= corr[nt][h];
+                    acc[nt][j][2 + h] *= corr[nt][h];
+                }
+            }
+
+        // ---------------- O^T += V^T P'^T, two k-chunks of 16 tokens ----------------
 #pragma unroll
         for (int kc = 0; kc < 2; ++kc) {
-            float vs4[4];
-            uint32_t vh[4][8];  // half2 pairs (jA(p), jB(p)) of d = 16 gq + j, for the lane's 4 tokens
+            // P'^T B fragments: (row g, tokens 16kc + 2q, +1) and (+8)
+            float vsA = 0.f, vsB = 0.f;
+            {
+                const int rA = 16 * kc + g, rB = rA + 8;
+                if (t0 + rA < t_hi) vsA = vsc_s[rA];
+                if (t0 + rB < t_hi) vsB = vsc_s[rB];
+                if constexpr (KV == 4) {
+                    vsA = __uint_as_float(__float_as_uint(vsA) & 0xFFFFFFF0u);
+                    vsB = __uint_as_float(__float_as_uint(vsB) & 0xFFFFFFF0u);
+                    if (ex_tile) {
+                        if (t0 + rA < t_hi && exact_of(t0 + rA) >= 0) vsA = 1.f;
+                        if (t0 + rB < t_hi && exact_of(t0 + rB) >= 0) vsB = 1.f;
+                    }
+                }
+            }
+            uint32_t pb[NT][2];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int r = 16 * kc + 2 * tq + (i & 1) + 8 * (i >> 1);
-                const int t = t0 + r;
-                vs4[i] = 0.f;
+            for (int nt = 0; nt < NT; ++nt) {
+                pb[nt][0] = movm_t(h2_as_u32(__floats2half2_rn(s[nt][kc][0] * vsA, s[nt][kc][1] * vsA)));
+                pb[nt][1] = movm_t(h2_as_u32(__floats2half2_rn(s[nt][kc][2] * vsB, s[nt][kc][3] * vsB)));
+            }
+            // V^T A fragments: tokens T0..T3 = 16kc + (2q, 2q+1, 2q+8, 2q+9); m-tile j rows g / g+8 are
+            // d = 16g + 2j / 16g + 2j + 1.  va[j][0..3] = (a0, a1, a2, a3)
+            uint32_t va[8][4];
+            const int rT[4] = {16 * kc + 2 * q, 16 * kc + 2 * q + 1, 16 * kc + 2 * q + 8, 16 * kc + 2 * q + 9};
+            bool slow = false;
+            if constexpr (KV == 4) slow = ex_tile;
+            if (!slow) {
+                if constexpr (KV == 8) {
+                    uint32_t w[4][4];
 #pragma unroll
-                for (int p = 0; p < 8; ++p) vh[i][p] = 0u;
-                if (t < t_hi) {
+                    for (int T = 0; T < 4; ++T) {
+                        uint4 v4 = make_uint4(0u, 0u, 0u, 0u);
+                        if (t0 + rT[T] < t_hi) v4 = chunk_at(1, rT[T], g);
+                        w[T][0] = v4.x ^ 0x80808080u; w[T][1] = v4.y ^ 0x80808080u;
+                        w[T][2] = v4.z ^ 0x80808080u; w[T][3] = v4.w ^ 0x80808080u;
+                    }
+                    const __half2 off = u32_as_h2(0x64806480u);  // 1152
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t sel = (j & 1) ? 0x7362u : 0x5140u;
+#pragma unroll
+                        for (int pr = 0; pr < 2; ++pr) {  // token pairs (T0, T1) and (T2, T3)
+                            const uint32_t x = prmt(w[2 * pr][j >> 1], w[2 * pr + 1][j >> 1], sel);
+                            va[j][2 * pr] = h2_as_u32(__hsub2(u32_as_h2(prmt(x, 0x64646464u, 0x5140u)), off));
+                            va[j][2 * pr + 1] = h2_as_u32(__hsub2(u32_as_h2(prmt(x, 0x64646464u, 0x7362u)), off));
+                        }
+                    }
+                } else {
+                    uint32_t w[4][2], zpp[2];
+#pragma unroll
+                    for (int T = 0; T < 4; ++T) {
+                        uint4 v4 = make_uint4(0u, 0u, 0u, 0u);
+                        if (t0 + rT[T] < t_hi) v4 = chunk_at(1, rT[T], g >> 1);
+                        w[T][0] = (g & 1) ? v4.z : v4.x;
+                        w[T][1] = (g & 1) ? v4.w : v4.y;
+                    }
+#pragma unroll
+                    for (int pr = 0; pr < 2; ++pr) {
+                        const int rA = rT[2 * pr], rB = rT[2 * pr + 1];
+                        const uint32_t za = (t0 + rA < t_hi) ? (__float_as_uint(vsc_s[rA]) & 0xFu) : 0u;
+                        const uint32_t zb = (t0 + rB < t_hi) ? (__float_as_uint(vsc_s[rB]) & 0xFu) : 0u;
+                        zpp[pr] = (0x6400u | za) | ((0x6400u | zb) << 16);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk += 2) {  // bytes (kk, kk+1) of word i -> m-tiles 4i+kk, 4i+kk+1
+                            const uint32_t sel = kk ? 0x7362u : 0x5140u;
+#pragma unroll
+                            for (int pr = 0; pr < 2; ++pr) {
+                                const uint32_t x = prmt(w[2 * pr][i], w[2 * pr + 1][i], sel);
+                                const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
+                                const __half2 z = u32_as_h2(zpp[pr]);
+                                va[4 * i + kk][2 * pr] = h2_as_u32(__hsub2(u32_as_h2(prmt(lo, 0x64646464u, 0x5140u)), z));
+                                va[4 * i + kk][2 * pr + 1] = h2_as_u32(__hsub2(u32_as_h2(prmt(hi, 0x64646464u, 0x5140u)), z));
+                                va[4 * i + kk + 1][2 * pr] = h2_as_u32(__hsub2(u32_as_h2(prmt(lo, 0x64646464u, 0x7362u)), z));
+                                va[4 * i + kk + 1][2 * pr + 1] = h2_as_u32(__hsub2(u32_as_h2(prmt(hi, 0x64646464u, 0x7362u)), z));
+                            }
+                        }
+                }
+            } else {
+                // int4 tile with exact rows: each token's 16 values (d = 16g .. 16g+15) as 8 half2
+                // (d, d+1), then paired across tokens
+                uint32_t nat[4][8];
+#pragma unroll
+                for (int T = 0; T < 4; ++T) {
+                    const int t = t0 + rT[T];
+#pragma unroll
+                    for (int p = 0; p < 8; ++p) nat[T][p] = 0u;
+                    if (t >= t_hi) continue;
                     const int e = exact_of(t);
                     if (e >= 0) {
                         const uint4* ep = reinterpret_cast<const uint4*>(
-                            a.exact_v + (((int64_t)rs * kExactRows + e) * a.num_kv_heads + kvh) * kHD + 16 * gq);
+                            a.exact_v + (((int64_t)rs * kExactRows + e) * a.num_kv_heads + kvh) * kHD + 16 * g);
                         const uint4 h0 = ep[0], h1 = ep[1];
-                        const uint32_t nat[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};  // (2p, 2p+1)
-                        // re-pair into the int4 layout (j, j+4), j = 8(p/4) + p%4: v[j] and v[j+4]
-                        // sit in the same half of nat[j/2] and nat[j/2 + 2]
-#pragma unroll
-                        for (int p = 0; p < 8; ++p) {
-                            const int j = 8 * (p / 4) + p % 4;
-                            vh[i][p] = __byte_perm(nat[j / 2], nat[j / 2 + 2], (j & 1) ? 0x7632u : 0x5410u);
-                        }
-                        vs4[i] = 1.f;
-                    } else if constexpr (KV == 8) {
-                        const uint4 w4 = chunk_at(1, r, gq);
-                        const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) i8x4_to_h2(w[c], vh[i][2 * c], vh[i][2 * c + 1]);
-                        vs4[i] = vsc_s[r];
+                        nat[T][0] = h0.x; nat[T][1] = h0.y; nat[T][2] = h0.z; nat[T][3] = h0.w;
+                        nat[T][4] = h1.x; nat[T][5] = h1.y; nat[T][6] = h1.z; nat[T][7] = h1.w;
                     } else {
-                        // this lane's 8 bytes (d = 16 gq .. 16 gq + 15) are the half gq & 1 of chunk gq / 2
-                        const uint4 w4 = chunk_at(1, r, gq >> 1);
-                        const uint32_t w[2] = {(gq & 1) ? w4.z : w4.x, (gq & 1) ? w4.w : w4.y};
-                        const uint32_t sb = __float_as_uint(vsc_s[r]);
-                        const uint32_t zp = 0x6400u | (sb & 0xFu);
-                        const uint32_t zp2 = zp | (zp << 16);
+                        const uint4 v4 = chunk_at(1, rT[T], g >> 1);
+                        const uint32_t ww[2] = {(g & 1) ? v4.z : v4.x, (g & 1) ? v4.w : v4.y};
+                        const uint32_t zp = 0x6400u | (__float_as_uint(vsc_s[rT[T]]) & 0xFu);
+                        const __half2 z = u32_as_h2(zp | (zp << 16));
 #pragma unroll
-                        for (int p = 0; p < 8; ++p) vh[i][p] = nib_pair(w[p / 4], p % 4, zp2);
-                        vs4[i] = __uint_as_float(sb & 0xFFFFFFF0u);
+                        for (int p = 0; p < 8; ++p) {  // byte p: (d = 16g + 2p low nibble, 2p + 1 high)
+                            const uint32_t b = (ww[p >> 2] >> (8 * (p & 3))) & 0xFFu;
+                            const uint32_t v = (b & 0xFu) | ((b >> 4) << 16) | 0x64006400u;
+                            nat[T][p] = h2_as_u32(__hsub2(u32_as_h2(v), z));
+                        }
                     }
                 }
-            }
-            uint32_t pa[4];
-            pa[0] = h2_as_u32(__floats2half2_rn(s[2 * kc][0] * vs4[0], s[2 * kc][1] * vs4[1]));
-            pa[1] = h2_as_u32(__floats2half2_rn(s[2 * kc][2] * vs4[0], s[2 * kc][3] * vs4[1]));
-            pa[2] = h2_as_u32(__floats2half2_rn(s[2 * kc + 1][0] * vs4[2], s[2 * kc + 1][1] * vs4[3]));
-            pa[3] = h2_as_u32(__floats2half2_rn(s[2 * kc + 1][2] * vs4[2], s[2 * kc + 1][3] * vs4[3]));
 #pragma unroll
-            for (int p = 0; p < 8; ++p) {
-                // b0 of n-tile j = (token 2tq, token 2tq+1) at j; b1 = (2tq+8, 2tq+9)
-                const uint32_t bA0 = __byte_perm(vh[0][p], vh[1][p], 0x5410);  // jA
-                const uint32_t bB0 = __byte_perm(vh[0][p], vh[1][p], 0x7632);  // jB
-                const uint32_t bA1 = __byte_perm(vh[2][p], vh[3][p], 0x5410);
-                const uint32_t bB1 = __byte_perm(vh[2][p], vh[3][p], 0x7632);
-                mma_16816(acc[Tr::jA(p)], pa, bA0, bA1);
-                mma_16816(acc[Tr::jB(p)], pa, bB0, bB1);
+                for (int j = 0; j < 8; ++j)
+#pragma unroll
+                    for (int pr = 0; pr < 2; ++pr) {
+                        va[j][2 * pr] = prmt(nat[2 * pr][j], nat[2 * pr + 1][j], 0x5410u);      // d = 16g + 2j
+                        va[j][2 * pr + 1] = prmt(nat[2 * pr][j], nat[2 * pr + 1][j], 0x7632u);  // d + 1
+                    }
             }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    mma_f16(acc[nt][j], va[j][0], va[j][1], va[j][2], va[j][3], pb[nt][0], pb[nt][1]);
         }
         __syncwarp();  // the ring slot of this tile is refilled next iteration
     }
     cp_async_wait<0>();
 
     // ---- partial of this split: acc (d order restored), m, l ----
-    // lane (g, q) holds for row g: d = 32q + j (acc[j][0]) and 32q + 16 + j (acc[j][1]); row g+8: [2], [3]
+    // acc[nt][j][h] is (d = 16g + 2j, row 2q + h), acc[nt][j][2 + h] is (d = 16g + 2j + 1, row 2q + h)
 #pragma unroll
-    for (int hrow = 0; hrow < 2; ++hrow) {
-        const int r = hrow ? r_hi : r_lo;
-        if (r >= rows) continue;
-        const int64_t tok = q0 + r / G;
-        const int hq = kvh * G + r % G;
-        float* dst = a.partial + ((tok * a.num_q_heads + hq) * a.num_splits + split) * kPartialStride;
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            float4* d4 = reinterpret_cast<float4*>(dst + 32 * tq + 16 * half);
+        for (int h = 0; h < 2; ++h) {
+            const int r = rbase + 8 * nt + 2 * q + h;
+            if (r >= rows) continue;
+            const int64_t tok = q0 + r / G;
+            const int hq = kvh * G + r % G;
+            float* dst = a.partial + ((tok * a.num_q_heads + hq) * a.num_splits + split) * kPartialStride;
+            float4* d4 = reinterpret_cast<float4*>(dst + 16 * g);
 #pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4)
-                d4[j4] = make_float4(acc[4 * j4][2 * hrow + half], acc[4 * j4 + 1][2 * hrow + half],
-                                     acc[4 * j4 + 2][2 * hrow + half], acc[4 * j4 + 3][2 * hrow + half]);
+            for (int k4 = 0; k4 < 4; ++k4)
+                d4[k4] = make_float4(acc[nt][2 * k4][h], acc[nt][2 * k4][2 + h], acc[nt][2 * k4 + 1][h],
+                                     acc[nt][2 * k4 + 1][2 + h]);
+            if (g == 0) {
+                // m is kept in the log2 domain; the reduce works in natural units
+                dst[kHD] = m_i[nt][h] * 0.6931471805599453f;
+                dst[kHD + 1] = l_i[nt][h];
+            }
         }
-        if (tq == 0) {
-            dst[kHD] = m_i[hrow];
-            dst[kHD + 1] = l_i[hrow];
-        }
-    }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -682,18 +815,18 @@ static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len) {
     return std::max(1, std::min(kMaxSplits, std::min(want, by_len)));
 }
 
-template <int KV, int MT>
-static cudaError_t launch_attn(dim3 grid, const KvAttnArgs& a, cudaStream_t st) {
-    const int smem = MT * AttnSmem<KV>::kWarpBytes;
+template <int KV, int NT>
+static cudaError_t launch_attn(dim3 grid, int warps, const KvAttnArgs& a, cudaStream_t st) {
+    const int smem = 2 * AttnSmem<KV>::kWarpBytes;  // sized for the largest launch (2 warps)
     static std::once_flag once[64];
     static cudaError_t attr_err[64];
     int dev = 0;
     cudaGetDevice(&dev);
     std::call_once(once[dev & 63], [&] {
-        attr_err[dev & 63] = cudaFuncSetAttribute(kv_attn_kernel<KV, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        attr_err[dev & 63] = cudaFuncSetAttribute(kv_attn_kernel<KV, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     });
     if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
-    kv_attn_kernel<KV, MT><<<grid, 32 * MT, smem, st>>>(a);
+    kv_attn_kernel<KV, NT><<<grid, 32 * warps, warps * AttnSmem<KV>::kWarpBytes, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -811,10 +944,17 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     a.exact_k = reinterpret_cast<const __half*>(exact_k); a.exact_v = reinterpret_cast<const __half*>(exact_v);
     a.exact_tag = exact_tag; a.seq_slots = seq_slots;
     const dim3 grid(num_seqs, num_kv_heads, S);
-    const bool two = max_q_len * G > 16;
+    // query rows per (sequence, KV head): up to 24 in one warp (8 per n-tile), 32 in two warps of 16
+    const int rows = max_q_len * G;
+    const int nt = rows <= 8 ? 1 : rows <= 16 ? 2 : rows <= 24 ? 3 : 2;
+    const int warps = rows <= 24 ? 1 : 2;
     cudaError_t e;
-    if (kv == 8) e = two ? launch_attn<8, 2>(grid, a, st) : launch_attn<8, 1>(grid, a, st);
-    else e = two ? launch_attn<4, 2>(grid, a, st) : launch_attn<4, 1>(grid, a, st);
+    if (kv == 8)
+        e = nt == 1 ? launch_attn<8, 1>(grid, warps, a, st) : nt == 2 ? launch_attn<8, 2>(grid, warps, a, st)
+                                                                     : launch_attn<8, 3>(grid, warps, a, st);
+    else
+        e = nt == 1 ? launch_attn<4, 1>(grid, warps, a, st) : nt == 2 ? launch_attn<4, 2>(grid, warps, a, st)
+                                                                     : launch_attn<4, 3>(grid, warps, a, st);
     if (e != cudaSuccess) return cuda_status(e);
     KvReduceArgs r = {};
     r.partial = a.partial; r.out = reinterpret_cast<__half*>(out); r.seq_lens = seq_lens;
