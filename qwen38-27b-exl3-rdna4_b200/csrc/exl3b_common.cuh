@@ -201,6 +201,14 @@ EXL3B_DEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uin
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// the same without `volatile`, so that the compiler schedules it freely among the decode
+EXL3B_DEV void mma_16816_nv(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 EXL3B_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 EXL3B_DEV void mbar_init(uint32_t bar, uint32_t count) {
@@ -234,6 +242,23 @@ EXL3B_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
     while (!mbar_try_wait(bar, parity)) {
         if (clock64() - t0 > kWaitCycles) {
             if (err) atomicExch(err, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+// The same wait, but it also gives up (without recording an error) as soon as another warp of
+// the CTA has raised *abort: a CTA whose wait failed stops within one try instead of one limit per
+// remaining barrier.  The fast path is a single try_wait.
+EXL3B_DEV bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, int* err, int code, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort != 0) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            if (err) atomicExch(err, code);
+            *abort = 1;
             return false;
         }
     }

@@ -1,50 +1,66 @@
 // The EXL3 linear for 1 <= m <= 16 rows (decode and speculative verify), fused end to end:
 //
-//   launch 1  had_in:  A_had = fp16(H128 * fp16(x * suh) / sqrt(128))  -> workspace, stored in the
-//                      mma B-fragment order, block-major [group][k/128][m][kAhadRow halves]
-//   launch 2  gemv:    stream-K over units of (128 output columns x 128 inputs); a producer warp
-//                      streams trellis rows and A_had blocks into a shared-memory ring of up to 8
-//                      stages with bulk async copies (no multicast); eight consumer warps decode the
-//                      trellis in registers straight into mma.m16n8k16 A fragments (W^T x A_had^T,
-//                      fp32 accumulate) and hand each finished column block to an epilogue warp,
-//                      which reduces it across the CTAs that shared it (partials in the workspace,
-//                      fixed summation order, last arriver finishes) and applies had_out + svh.
+//   launch 1  had_in:  A_had = fp16(H128 * fp16(x * suh) / sqrt(128)) -> workspace, k-tile-major
+//                      [group][k/16][m][16 halves] with each 16-half row in mma B-fragment order
+//   launch 2  gemv:    stream-K over units of R trellis k-tile rows x one super-block of up to
+//                      1024 output columns (64 n-tiles).  In the checkpoint layout
+//                      [k/16][n/16][16K] a unit row is one contiguous run of up to 64 x 32K
+//                      bytes (8 KB at K = 4), so a producer warp fetches a unit with R + 1 bulk
+//                      copies (no multicast) into a shared-memory ring.  Sixteen decode warps
+//                      decode the trellis in registers straight into mma.m16n8k16 A fragments
+//                      (W^T x A_had^T, fp32 accumulate); warp w owns n-tiles w, w+16, w+32, w+48 of
+//                      the super-block.  When the CTA leaves a super-block the decode warps pool
+//                      their accumulators in a shared-memory tile and warp b takes column block b:
+//                      it reduces the block across the CTAs that shared it (partials in the
+//                      workspace, fixed summation order, last arriver finishes) and applies
+//                      had_out + svh.
 //   Launch 2 is a programmatic dependent launch: its trellis copies start while launch 1 runs.
 //
 // Reference semantics: reference/exl3_oracle.py:307-351 (gemv_mul1, all codebooks);
 // kernels replaced: exl3_gemm / exl3_gemv_mr / exl3_mgemm / exl3_gemv_mr_grouped of the fork
 // (vllm_plugin/exl3rocm/ops.py:80-85,134-170; 0002-gemv-multirow.patch:79-88 for the rule that
 // every row equals the m = 1 result bit for bit: here the work partition depends only on
-// (k, n, groups) and each mma column is one input row, so rows never interact).
+// (k, n, groups, K) and each mma column is one input row, so rows never interact).
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "exl3b_common.cuh"
 
 namespace exl3b {
 
-constexpr int kConsumerWarps = 8;  // warp w: n-tiles 2(w%4), 2(w%4)+1; k-tiles 4(w/4)..+3 of a unit
-constexpr int kThreads = (kConsumerWarps + 2) * 32;  // + producer warp + epilogue warp
-// One A_had row of a unit: 8 k-tiles x 16 fp16 in B-fragment order (256 B) + 32 B of padding, so
-// that the eight rows a warp reads at once fall in distinct banks.
-constexpr int kAhadRow = 144;  // halves
+constexpr int kDecodeWarps = 16;
+constexpr int kProducerWarp = kDecodeWarps;
+constexpr int kThreads = (kDecodeWarps + 1) * 32;
+constexpr int kFlushBar = 1;      // named barrier of the decode warps
+constexpr int kMaxBatch = 8;      // partials a finishing warp loads before summing them
+constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
+constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
+
+// trellis k-tile rows per unit: about 32 KB of trellis per stage
+__host__ __device__ constexpr int rows_per_unit(int K) { return K <= 2 ? 8 : (K <= 4 ? 4 : 2); }
 
 struct GemvGroups {
     const uint16_t* trellis[EXL3B_MAX_GROUPS];
     const __half* svh[EXL3B_MAX_GROUPS];
     __half* y[EXL3B_MAX_GROUPS];
     int n_tiles[EXL3B_MAX_GROUPS];
-    int blk_prefix[EXL3B_MAX_GROUPS + 1];  // first global column block of each group
+    int blk_prefix[EXL3B_MAX_GROUPS + 1];  // first global 128-column block of each group
+    int sb_prefix[EXL3B_MAX_GROUPS + 1];   // first global super-block of each group
+    int sb_base[EXL3B_MAX_GROUPS];         // column blocks per super-block (the first sb_extra get one more)
+    int sb_extra[EXL3B_MAX_GROUPS];
 };
 
 struct GemvParams {
     GemvGroups g;
     const __half* a_had;  // workspace
-    float* partials;      // workspace: [2 * P][m][128]
+    float* partials;      // workspace: [ctas + super-blocks - 1][m][sb_cols], slot = cta + super-block
     int* counters;        // workspace: one per global column block
     int* err;             // workspace error word
-    int groups, m, nk;    // nk = k / 128
-    int units, ctas;      // U = total column blocks * nk, P
+    int groups, m, kt;    // kt = k / 16
+    int ku;               // units per super-block = kt / R
+    int units, ctas;
+    int sb_cols;          // widest super-block of the call, in columns
     int64_t ldy;
 };
 
@@ -53,14 +69,14 @@ struct HadInParams {
 };
 
 // ---------------------------------------------------------------------------------------------
-// launch 1: input transform, one warp per (row, k-block, group)
+// launch 1: input transform, one warp per (row, k-block of 128, group)
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) had_in_kernel(const __half* __restrict__ x, int m, int k,
                                                      const __grid_constant__ HadInParams p,
                                                      __half* __restrict__ a_had) {
     griddep_launch();
     const int row = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j = blockIdx.x, g = blockIdx.y, nk = k >> 7;
+    const int j = blockIdx.x, g = blockIdx.y;
     if (row >= m) return;
     const int c = j * 128 + 4 * lane;
     const uint2 xr = *reinterpret_cast<const uint2*>(x + (int64_t)row * k + c);
@@ -71,12 +87,11 @@ __global__ void __launch_bounds__(512) had_in_kernel(const __half* __restrict__ 
     had128_warp(v);
     const uint32_t h01 = h2_as_u32(__floats2half2_rn(v[0] * kRScale, v[1] * kRScale));
     const uint32_t h23 = h2_as_u32(__floats2half2_rn(v[2] * kRScale, v[3] * kRScale));
-    // element e = 4*lane + s lives in k-tile e/16 at fragment slot of kk = e%16:
+    // element e = 4*lane + s sits in k-tile 8j + e/16 at the fragment slot of kk = e%16:
     // kk = 2q + b -> 4q + b (kk < 8);  kk = 8 + 2q + b -> 4q + 2 + b
     const int kt = lane >> 2, kq = lane & 3;
     const int base = (kq < 2) ? 8 * kq : 8 * (kq - 2) + 2;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(
-        a_had + ((int64_t)(g * nk + j) * m + row) * kAhadRow + kt * 16);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(a_had + (((int64_t)g * (k / 16) + 8 * j + kt) * m + row) * 16);
     dst[base >> 1] = h01;
     dst[(base + 4) >> 1] = h23;
 }
@@ -87,76 +102,64 @@ __global__ void __launch_bounds__(512) had_in_kernel(const __half* __restrict__ 
 EXL3B_DEV int unit_start(int c, int U, int P) { return (int)(((int64_t)c * U) / P); }
 EXL3B_DEV int cta_of_unit(int u, int U, int P) { return (int)((((int64_t)u + 1) * P - 1) / U); }
 
-// slot of CTA c's partial for global block B: 0 if B is the block its range starts in, else 1
-EXL3B_DEV int partial_slot(int c, int B, int nk, int U, int P) {
-    return 2 * c + ((unit_start(c, U, P) / nk) == B ? 0 : 1);
-}
+struct SbInfo {
+    int g;     // group
+    int b0;    // first 128-column block of the super-block, inside the group
+    int nblk;  // its column blocks
+};
 
-EXL3B_DEV int group_of_block(const GemvGroups& gg, int groups, int B) {
+EXL3B_DEV SbInfo sb_info(const GemvGroups& gg, int groups, int sb) {
     int g = 0;
-    while (g + 1 < groups && B >= gg.blk_prefix[g + 1]) ++g;
-    return g;
+    while (g + 1 < groups && sb >= gg.sb_prefix[g + 1]) ++g;
+    const int i = sb - gg.sb_prefix[g];
+    const int base = gg.sb_base[g], extra = gg.sb_extra[g];
+    return {g, i * base + min(i, extra), base + (i < extra ? 1 : 0)};
 }
 
 // ---------------------------------------------------------------------------------------------
 // launch 2: the stream-K decode GEMV
 // ---------------------------------------------------------------------------------------------
-// Shared memory per CTA: a ring of kStages stages (one unit each: 8 trellis rows + the unit's
-// A_had rows, MT*8 rows of kAhadRow halves, rows >= m zero), a double-buffered fp32 accumulator
-// tile [2 buffers][2 k-halves][MT*8 rows][128] handed from the consumers to the epilogue warp,
-// and the mbarriers.  kStages is chosen so that two CTAs fit on an SM.
+// Shared memory: a ring of kStages stages (R trellis rows of up to 64 tiles at a fixed stride,
+// then the unit's A_had rows), the fp32 accumulator tile [8 MT rows][kAccCols] where the decode
+// warps pool a finished super-block, and the mbarriers.
 template <int K, int MT>
 struct GemvSmem {
-    static constexpr int kTrellisStage = 2048 * K;  // 8 k-tiles x 8 n-tiles x 32K bytes
-    static constexpr int kRows = 8 * MT;
-    static constexpr int kAhadBytes = kRows * kAhadRow * 2;
-    static constexpr int kStageBytes = kTrellisStage + kAhadBytes;
-    static constexpr int kAccBuf = 2 * kRows * 128 * 4;  // two k-halves
-    static constexpr int kAccBytes = 2 * kAccBuf;
-    static constexpr int kBudget = 110 * 1024;
-    static constexpr int kStages0 = (kBudget - kAccBytes - 256) / kStageBytes;
-    static constexpr int kStages = kStages0 > 8 ? 8 : (kStages0 < 2 ? 2 : kStages0);
+    static constexpr int R = rows_per_unit(K);
+    static constexpr int kTile = 32 * K;                  // bytes of one 16x16 tile
+    static constexpr int kRowBytes = kSbTiles * kTile;    // stride of the unit's rows in a stage
+    static constexpr int kTrellisStage = R * kRowBytes;
+    static constexpr int kAhadStage = R * 8 * MT * 32;    // R k-tiles x 8 MT rows x 16 halves
+    static constexpr int kStageBytes = kTrellisStage + kAhadStage;
+    static constexpr int kAccBytes = 8 * MT * kAccCols * 4;
+    static constexpr int kBudget = 220 * 1024;
+    static constexpr int kStages0 = (kBudget - kAccBytes - 512) / kStageBytes;
+    static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
+    static_assert(kStages >= 2, "shared-memory ring too small");
     static constexpr int kAccOffset = kStages * kStageBytes;
-    static constexpr int kBarOffset = kAccOffset + kAccBytes;  // full[S], empty[S], accf[2], acce[2]
-    static constexpr int kFlagOffset = kBarOffset + (2 * kStages + 4) * 8;
+    static constexpr int kBarOffset = kAccOffset + kAccBytes;  // full[S], empty[S]
+    static constexpr int kFlagOffset = kBarOffset + 2 * kStages * 8;
     static constexpr int kTotal = kFlagOffset + 16;
 };
 
-constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kEpilogueWarp = kConsumerWarps + 1;
-
 template <int K, int CB, int MT>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     using S = GemvSmem<K, MT>;
     constexpr int kStages = S::kStages;
+    constexpr int R = S::R;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t full0 = sbase + S::kBarOffset, empty0 = full0 + kStages * 8;
-    const uint32_t accf0 = empty0 + kStages * 8, acce0 = accf0 + 16;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kFlagOffset);
 
-    const int c = blockIdx.x, P = p.ctas, U = p.units, nk = p.nk, m = p.m;
+    const int c = blockIdx.x, P = p.ctas, U = p.units, ku = p.ku, m = p.m;
     const int u0 = unit_start(c, U, P), u1 = unit_start(c + 1, U, P);
     const int nunits = u1 - u0;
 
-    // A_had rows m..kRows-1 are never written by the copies: zero them once so the consumers'
-    // B fragments read zeros there without predicates
-    {
-        const int zero_words = (S::kRows - m) * kAhadRow / 2;
-        for (int s = 0; s < kStages; ++s) {
-            uint32_t* z = reinterpret_cast<uint32_t*>(smem + s * S::kStageBytes + S::kTrellisStage + m * kAhadRow * 2);
-            for (int i = threadIdx.x; i < zero_words; i += kThreads) z[i] = 0u;
-        }
-    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, kConsumerWarps);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(accf0 + 8 * b, kConsumerWarps);
-            mbar_init(acce0 + 8 * b, 1);
+            mbar_init(empty0 + 8 * s, kDecodeWarps);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -165,35 +168,37 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
 
     if (warp == kProducerWarp) {
         // ------------------------------ producer warp ------------------------------
-        const uint32_t ahad_bytes = (uint32_t)m * kAhadRow * 2;
         bool waited_dep = false;
         int issued = 0;
-        int B = u0 / nk, j = u0 % nk;
-        int g = group_of_block(p.g, p.groups, B);
+        int sb = -1;
+        SbInfo si = {0, 0, 0};
         for (int i = 0; i < nunits; ++i) {
             const int s = i % kStages, n = i / kStages;
             bool ok = true;
             if (n > 0) ok = mbar_wait(empty0 + 8 * s, (n - 1) & 1, p.err, 1);
             if (!ok) *abort_flag = 1;
             if (__any_sync(0xFFFFFFFFu, *abort_flag != 0)) break;
-            const int b = B - p.g.blk_prefix[g];
+            const int u = u0 + i;
+            if (u / ku != sb) {
+                sb = u / ku;
+                si = sb_info(p.g, p.groups, sb);
+            }
+            const int kr0 = (u - sb * ku) * R;
+            const uint32_t row_bytes = (uint32_t)si.nblk * 8 * S::kTile;
+            const uint32_t ahad_bytes = (uint32_t)(R * m * 32);
             const uint32_t st = sbase + s * S::kStageBytes;
-            if (lane == 0) mbar_arrive_expect_tx(full0 + 8 * s, S::kTrellisStage + ahad_bytes);
+            if (lane == 0) mbar_arrive_expect_tx(full0 + 8 * s, R * row_bytes + ahad_bytes);
             __syncwarp();
-            if (lane < 8) {
-                const uint16_t* src = p.g.trellis[g] + ((int64_t)(j * 8 + lane) * p.g.n_tiles[g] + b * 8) * (16 * K);
-                bulk_g2s(st + lane * (256 * K), src, 256 * K, full0 + 8 * s);
-            } else if (lane == 8) {
+            if (lane < R) {
+                const uint16_t* src =
+                    p.g.trellis[si.g] + ((int64_t)(kr0 + lane) * p.g.n_tiles[si.g] + si.b0 * 8) * (16 * K);
+                bulk_g2s(st + lane * S::kRowBytes, src, row_bytes, full0 + 8 * s);
+            } else if (lane == R) {
                 if (!waited_dep) { griddep_wait(); waited_dep = true; }
-                const __half* src = p.a_had + (int64_t)(g * nk + j) * m * kAhadRow;
+                const __half* src = p.a_had + ((int64_t)si.g * p.kt + kr0) * m * 16;
                 bulk_g2s(st + S::kTrellisStage, src, ahad_bytes, full0 + 8 * s);
             }
             issued = i + 1;
-            if (++j == nk) {
-                j = 0;
-                ++B;
-                if (g + 1 < p.groups && B >= p.g.blk_prefix[g + 1]) ++g;
-            }
         }
         // No copy may still be landing in shared memory when the CTA exits: wait (bounded) for
         // the last fill of every stage.  Normally these completed long ago.
@@ -205,61 +210,151 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
 
     float* acc_s = reinterpret_cast<float*>(smem + S::kAccOffset);
 
-    if (warp == kEpilogueWarp) {
-        // ------------------------------ epilogue warp ------------------------------
-        // Walks the same column blocks the consumers flush, in the same order.  For each: sum the
-        // two k-halves; if this CTA covered the whole block, transform and store; otherwise
-        // publish the partial and, if it is the last of the block's CTAs to arrive, gather all
-        // partials in fixed CTA order and finish the block.
-        const int B_first = u0 / nk, B_last = (u1 - 1) / nk;
-        const int col = 4 * lane;
-        for (int Bc = B_first, f = 0; Bc <= B_last; ++Bc, ++f) {
-            const int fb = f & 1;
-            bool ok = (*abort_flag == 0) && mbar_wait(accf0 + 8 * fb, (f >> 1) & 1, p.err, 4);
-            if (!ok) *abort_flag = 1;
-            const bool live = !__any_sync(0xFFFFFFFFu, *abort_flag != 0);
-            const float* ab = acc_s + fb * (S::kAccBuf / 4);
-            const int seg_lo = max(u0, Bc * nk), seg_hi = min(u1, (Bc + 1) * nk);
-            const bool whole = (seg_lo == Bc * nk) && (seg_hi == (Bc + 1) * nk);
-            const int cf = cta_of_unit(Bc * nk, U, P), cl = cta_of_unit((Bc + 1) * nk - 1, U, P);
-            bool finalize = whole;
-            if (live && !whole) {
-                float* mine = p.partials + (int64_t)partial_slot(c, Bc, nk, U, P) * m * 128;
-                for (int row = 0; row < m; ++row) {
-                    const float4 t0 = *reinterpret_cast<const float4*>(ab + row * 128 + col);
-                    const float4 t1 = *reinterpret_cast<const float4*>(ab + (S::kRows + row) * 128 + col);
-                    __stcg(reinterpret_cast<float4*>(mine + row * 128 + col),
-                           make_float4(t0.x + t1.x, t0.y + t1.y, t0.z + t1.z, t0.w + t1.w));
+    // ------------------------------ decode warps ------------------------------
+    LaneGeom<K> geom;
+    geom.init(lane);
+    const int gq = lane >> 2, tq = lane & 3;
+    // this warp's first tile (n-tile `warp` of row 0) plus the lane's word offsets; the other
+    // tiles of a unit sit at compile-time offsets from these
+    uint32_t woff[LaneGeom<K>::kNW];
+#pragma unroll
+    for (int q = 0; q < LaneGeom<K>::kNW; ++q) woff[q] = (uint32_t)(warp * S::kTile) + geom.off[q];
+    const uint32_t boff = (uint32_t)(S::kTrellisStage + gq * 32 + tq * 8);
+    const uint32_t mstride = (uint32_t)m * 32;  // A_had bytes per k-tile in a stage
+
+    float acc[MT][4][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
+    int sb = u0 / ku;
+    SbInfo si = sb_info(p.g, p.groups, sb);
+    int nj = 0;  // n-tiles of this warp in the current super-block
+    while (nj < 4 && warp + 16 * nj < si.nblk * 8) ++nj;
+
+    // one unit: R k-tile rows x this warp's n-tiles (all four when FULL, else the first nj)
+    auto unit = [&](const uint8_t* st, auto full_tag) {
+        constexpr bool FULL = decltype(full_tag)::value;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            uint32_t b[MT][2];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint2 v = *reinterpret_cast<const uint2*>(st + boff + r * mstride + mt * 8 * 32);
+                b[mt][0] = v.x;
+                b[mt][1] = v.y;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (FULL || j < nj) {
+                    uint32_t Wd[LaneGeom<K>::kNW];
+#pragma unroll
+                    for (int q = 0; q < LaneGeom<K>::kNW; ++q)
+                        Wd[q] = *reinterpret_cast<const uint32_t*>(st + woff[q] + r * S::kRowBytes + j * 16 * S::kTile);
+                    uint32_t a[4];
+                    lane_decode_frag<K, CB>(Wd, geom.phi, a);
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) mma_16816_nv(acc[mt][j], a, b[mt][0], b[mt][1]);
                 }
+            }
+        }
+    };
+
+    for (int i = 0; i < nunits; ++i) {
+        const int s = i % kStages, n = i / kStages;
+        // On a wait that gives up, the warps keep walking the units without touching the ring,
+        // so every barrier below still sees all of its arrivals.
+        const bool ok = mbar_wait_or_abort(full0 + 8 * s, n & 1, p.err, 3, abort_flag);
+        if (__all_sync(0xFFFFFFFFu, ok)) {
+            const uint8_t* st = smem + s * S::kStageBytes;
+            // the unguarded copy only where registers allow it (one m-tile)
+            if (MT == 1 && nj == 4) unit(st, std::true_type{});
+            else if (nj > 0) unit(st, std::false_type{});
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
+
+        const int u = u0 + i;
+        const bool sb_end = (u + 1) % ku == 0 || i == nunits - 1;
+        if (!sb_end) continue;
+
+        // ---------------- pool the finished super-block, then one warp per column block ----------------
+        named_bar(kFlushBar, kDecodeWarps * 32);  // the previous flush's readers are done with acc_s
+        // fragment -> acc_s[row][col]: lane (gq, tq) holds D[col gq (+8)][rows 2tq, 2tq+1] of n-tile
+        // warp + 16 j
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j < nj) {
+                    const int col = (warp + 16 * j) * 16 + gq;
+                    const int r0 = 8 * mt + 2 * tq;
+                    if (r0 < m) {
+                        acc_s[r0 * kAccCols + col] = acc[mt][j][0];
+                        acc_s[r0 * kAccCols + col + 8] = acc[mt][j][2];
+                    }
+                    if (r0 + 1 < m) {
+                        acc_s[(r0 + 1) * kAccCols + col] = acc[mt][j][1];
+                        acc_s[(r0 + 1) * kAccCols + col + 8] = acc[mt][j][3];
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
+            }
+        named_bar(kFlushBar, kDecodeWarps * 32);
+        if (warp < si.nblk && *abort_flag == 0) {
+            // If this CTA covered the super-block's whole k range, transform and store; otherwise
+            // publish the partial and, if it is the last of the block's CTAs to arrive, gather all
+            // partials in fixed CTA order and finish the block.
+            const int blk = warp;
+            const int seg_lo = max(u0, sb * ku), seg_hi = min(u1, (sb + 1) * ku);
+            const bool whole = (seg_lo == sb * ku) && (seg_hi == (sb + 1) * ku);
+            const int cf = cta_of_unit(sb * ku, U, P), cl = cta_of_unit((sb + 1) * ku - 1, U, P);
+            const int Bg = p.g.blk_prefix[si.g] + si.b0 + blk;
+            const int col = blk * 128 + 4 * lane;  // column inside the super-block
+            bool finalize = whole;
+            if (!whole) {
+                // CTA ranges are contiguous and ordered, so cta + super-block is unique among the
+                // (CTA, super-block) pairs that meet
+                float* mine = p.partials + ((int64_t)(c + sb) * m) * p.sb_cols;
+                for (int row = 0; row < m; ++row)
+                    __stcg(reinterpret_cast<float4*>(mine + (int64_t)row * p.sb_cols + col),
+                           *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col));
                 __syncwarp();
                 int v = 0;
                 if (lane == 0) {
                     // cumulative fence over the warp's partial stores, then the counter; the
                     // second fence orders the reads of other CTAs' partials after it
                     __threadfence();
-                    v = atomicAdd(p.counters + Bc, 1);
+                    v = atomicAdd(p.counters + Bg, 1);
                     __threadfence();
                 }
                 v = __shfl_sync(0xFFFFFFFFu, v, 0);
                 finalize = (v == cl - cf);
             }
-            if (live && finalize) {
-                const int g = group_of_block(p.g, p.groups, Bc);
-                const int b = Bc - p.g.blk_prefix[g];
-                const uint2 sv = *reinterpret_cast<const uint2*>(p.g.svh[g] + b * 128 + col);
+            if (finalize) {
+                const int b = si.b0 + blk;
+                const uint2 sv = *reinterpret_cast<const uint2*>(p.g.svh[si.g] + b * 128 + 4 * lane);
                 for (int row = 0; row < m; ++row) {
                     float v[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int cc = cf; cc <= cl; ++cc) {  // fixed order: deterministic sums
-                        float4 t;
-                        if (cc == c) {
-                            const float4 t0 = *reinterpret_cast<const float4*>(ab + row * 128 + col);
-                            const float4 t1 = *reinterpret_cast<const float4*>(ab + (S::kRows + row) * 128 + col);
-                            t = make_float4(t0.x + t1.x, t0.y + t1.y, t0.z + t1.z, t0.w + t1.w);
-                        } else {
-                            t = __ldcg(reinterpret_cast<const float4*>(
-                                p.partials + ((int64_t)partial_slot(cc, Bc, nk, U, P) * m + row) * 128 + col));
+                    for (int c0 = cf; c0 <= cl; c0 += kMaxBatch) {
+                        // all loads of a batch in flight together, then summed in CTA order
+                        float4 t[kMaxBatch];
+#pragma unroll
+                        for (int q = 0; q < kMaxBatch; ++q) {
+                            const int cc = c0 + q;
+                            if (cc > cl) break;
+                            t[q] = (cc == c) ? *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col)
+                                             : __ldcg(reinterpret_cast<const float4*>(
+                                                   p.partials + ((int64_t)(cc + sb) * m + row) * p.sb_cols + col));
                         }
-                        v[0] += t.x; v[1] += t.y; v[2] += t.z; v[3] += t.w;
+#pragma unroll
+                        for (int q = 0; q < kMaxBatch; ++q) {
+                            if (c0 + q > cl) break;
+                            v[0] += t[q].x; v[1] += t[q].y; v[2] += t[q].z; v[3] += t[q].w;
+                        }
                     }
                     // c_rot is stored fp16 between the dot and the output transform (oracle :349-351)
                     const __half2 c01 = __floats2half2_rn(v[0], v[1]), c23 = __floats2half2_rn(v[2], v[3]);
@@ -269,108 +364,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                     __half2 y23 = __floats2half2_rn(h[2] * kRScale, h[3] * kRScale);
                     y01 = __hmul2(y01, u32_as_h2(sv.x));
                     y23 = __hmul2(y23, u32_as_h2(sv.y));
-                    *reinterpret_cast<uint2*>(p.g.y[g] + row * p.ldy + b * 128 + col) =
+                    *reinterpret_cast<uint2*>(p.g.y[si.g] + row * p.ldy + b * 128 + 4 * lane) =
                         make_uint2(h2_as_u32(y01), h2_as_u32(y23));
                 }
-                if (!whole && lane == 0) p.counters[Bc] = 0;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acce0 + 8 * fb);
-        }
-        return;
-    }
-
-    // ------------------------------ consumer warps ------------------------------
-    LaneGeom<K> geom;
-    geom.init(lane);
-    const int gq = lane >> 2, tq = lane & 3;
-    const int tpair = warp & 3, kh = warp >> 2;
-    // per-lane offsets inside a stage: this warp's first tile (k-tile 4kh, n-tile 2 tpair) plus the
-    // lane's word offsets; the remaining tiles are compile-time offsets from these
-    const uint32_t tile0 = (uint32_t)((kh * 4 * 8 + 2 * tpair) * 32 * K);
-    uint32_t woff[LaneGeom<K>::kNW];
-#pragma unroll
-    for (int q = 0; q < LaneGeom<K>::kNW; ++q) woff[q] = tile0 + geom.off[q];
-    const uint32_t boff = (uint32_t)(S::kTrellisStage + gq * kAhadRow * 2 + kh * 4 * 32 + tq * 8);
-
-    float acc[MT][2][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int jn = 0; jn < 2; ++jn)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[mt][jn][e] = 0.f;
-    int j = u0 % nk, nflush = 0;
-
-    for (int i = 0; i < nunits; ++i) {
-        const int s = i % kStages, n = i / kStages;
-        // On a wait that gives up, the warps keep walking the units without touching the ring,
-        // so every barrier below still sees all of its arrivals.
-        bool ok = (*abort_flag == 0) && mbar_wait(full0 + 8 * s, n & 1, p.err, 3);
-        if (!ok) *abort_flag = 1;
-        const bool live = !__any_sync(0xFFFFFFFFu, *abort_flag != 0);
-        if (live) {
-            const uint8_t* st = smem + s * S::kStageBytes;
-            const uint8_t* bp = st + boff;
-#pragma unroll
-            for (int kt = 0; kt < 4; ++kt) {
-                uint32_t b[MT][2];
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    const uint2 v = *reinterpret_cast<const uint2*>(bp + mt * 8 * kAhadRow * 2 + kt * 32);
-                    b[mt][0] = v.x;
-                    b[mt][1] = v.y;
-                }
-#pragma unroll
-                for (int jn = 0; jn < 2; ++jn) {
-                    constexpr int kTile = 32 * K;
-                    uint32_t Wd[LaneGeom<K>::kNW];
-#pragma unroll
-                    for (int q = 0; q < LaneGeom<K>::kNW; ++q)
-                        Wd[q] = *reinterpret_cast<const uint32_t*>(st + woff[q] + (kt * 8 + jn) * kTile);
-                    uint32_t a[4];
-                    lane_decode_frag<K, CB>(Wd, geom.phi, a);
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) mma_16816(acc[mt][jn], a, b[mt][0], b[mt][1]);
-                }
+                if (!whole && lane == 0) p.counters[Bg] = 0;
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * s);
-
-        const bool block_end = (++j == nk);
-        if (block_end) j = 0;
-        if (!block_end && i != nunits - 1) continue;
-
-        // ---------------- hand the finished block to the epilogue warp ----------------
-        // acc buffer fb is free once the epilogue released its previous use (two flushes ago)
-        const int fb = nflush & 1;
-        if (nflush >= 2) {
-            bool ok2 = (*abort_flag == 0) && mbar_wait(acce0 + 8 * fb, ((nflush >> 1) - 1) & 1, p.err, 5);
-            if (!ok2) *abort_flag = 1;
+        if (i + 1 < nunits) {
+            ++sb;
+            si = sb_info(p.g, p.groups, sb);
+            nj = 0;
+            while (nj < 4 && warp + 16 * nj < si.nblk * 8) ++nj;
         }
-        // fragment -> acc_s[fb][kh][row][col]: lane (gq, tq) holds D[col gq (+8)][rows 2tq, 2tq+1]
-        float* acc_h = acc_s + fb * (S::kAccBuf / 4) + kh * S::kRows * 128;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int jn = 0; jn < 2; ++jn) {
-                const int col = (2 * tpair + jn) * 16 + gq;
-                const int r0 = 8 * mt + 2 * tq;
-                acc_h[r0 * 128 + col] = acc[mt][jn][0];
-                acc_h[r0 * 128 + col + 8] = acc[mt][jn][2];
-                acc_h[(r0 + 1) * 128 + col] = acc[mt][jn][1];
-                acc_h[(r0 + 1) * 128 + col + 8] = acc[mt][jn][3];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[mt][jn][e] = 0.f;
-            }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(accf0 + 8 * fb);
-        ++nflush;
     }
 }
-
-// ---------------------------------------------------------------------------------------------
 
 // ---------------------------------------------------------------------------------------------
 // host side
@@ -396,23 +403,48 @@ static int num_sms() {
     return sms[dev];
 }
 
-// Stream-K width: two CTAs per SM, independent of m, K and codebook, so the partition (and
-// therefore every rounding) depends only on the layer shape.
-static int gemv_ctas(int units) { return std::min(units, 2 * num_sms()); }
+// Stream-K width: one CTA per SM, independent of m and codebook, so the partition (and therefore
+// every rounding) depends only on the layer shape and K.
+static int gemv_ctas(int units) { return std::min(units, num_sms()); }
+
+// Super-blocks of one group: its 128-column blocks split as evenly as possible into runs of at
+// most 8 (1024 columns).
+static void split_super_blocks(int blocks, int& count, int& base, int& extra) {
+    count = (blocks + 7) / 8;
+    base = blocks / count;
+    extra = blocks % count;
+}
+
+struct Partition {
+    int ku, units, ctas, sb_cols, super_blocks;
+};
+
+static Partition partition(int k, int K, int groups, const int* n) {
+    Partition q = {};
+    q.ku = (k / 16) / rows_per_unit(K);
+    int widest = 0;
+    for (int g = 0; g < groups; ++g) {
+        int cnt, base, extra;
+        split_super_blocks(n[g] / 128, cnt, base, extra);
+        q.super_blocks += cnt;
+        widest = std::max(widest, base + (extra ? 1 : 0));
+    }
+    q.sb_cols = widest * 128;
+    q.units = q.super_blocks * q.ku;
+    q.ctas = gemv_ctas(std::max(q.units, 1));
+    return q;
+}
 
 struct WsLayout {
     size_t counters, a_had, partials, total;
 };
 
-static WsLayout ws_layout(int m, int k, int groups, int64_t n_total) {
+static WsLayout ws_layout(int m, int k, int groups, const Partition& q) {
     WsLayout L;
-    const int64_t blocks = n_total / 128;
-    const int units = (int)(blocks * (k / 128));
-    const int P = gemv_ctas(std::max(units, 1));
     L.counters = kHeaderBytes;
     L.a_had = round_up(L.counters + kCounterBytes, 256);
-    L.partials = round_up(L.a_had + (size_t)groups * m * (k / 128) * kAhadRow * 2, 256);
-    L.total = round_up(L.partials + (size_t)2 * P * m * 128 * 4, 256);
+    L.partials = round_up(L.a_had + (size_t)groups * (k / 16) * m * 32, 256);
+    L.total = round_up(L.partials + (size_t)(q.ctas + q.super_blocks - 1) * m * q.sb_cols * 4, 256);
     return L;
 }
 
@@ -473,7 +505,8 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
         n_total += n[g];
     }
     if (n_total / 128 > kMaxBlocks) return EXL3B_DECLINED;
-    const WsLayout L = ws_layout(m, k, groups, n_total);
+    const Partition q = partition(k, K, groups, n);
+    const WsLayout L = ws_layout(m, k, groups, q);
     if (ws_bytes < L.total) return EXL3B_WORKSPACE;
 
     cudaStream_t st = (cudaStream_t)stream;
@@ -482,7 +515,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
 
     HadInParams hp = {};
     GemvParams p = {};
-    int blk = 0;
+    int blk = 0, sbs = 0;
     for (int g = 0; g < groups; ++g) {
         hp.suh[g] = reinterpret_cast<const __half*>(suh[g]);
         p.g.trellis[g] = trellis[g];
@@ -490,18 +523,27 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
         p.g.y[g] = reinterpret_cast<__half*>(y[g]);
         p.g.n_tiles[g] = n[g] / 16;
         p.g.blk_prefix[g] = blk;
+        p.g.sb_prefix[g] = sbs;
+        int cnt, base, extra;
+        split_super_blocks(n[g] / 128, cnt, base, extra);
+        p.g.sb_base[g] = base;
+        p.g.sb_extra[g] = extra;
         blk += n[g] / 128;
+        sbs += cnt;
     }
     p.g.blk_prefix[groups] = blk;
+    p.g.sb_prefix[groups] = sbs;
     p.a_had = a_had;
     p.partials = reinterpret_cast<float*>(ws + L.partials);
     p.counters = reinterpret_cast<int*>(ws + L.counters);
     p.err = reinterpret_cast<int*>(ws);
     p.groups = groups;
     p.m = m;
-    p.nk = k / 128;
-    p.units = blk * p.nk;
-    p.ctas = gemv_ctas(p.units);
+    p.kt = k / 16;
+    p.ku = q.ku;
+    p.units = q.units;
+    p.ctas = q.ctas;
+    p.sb_cols = q.sb_cols;
     p.ldy = ldy;
 
     had_in_kernel<<<dim3(k / 128, groups), dim3(32 * m), 0, st>>>(reinterpret_cast<const __half*>(x), m, k, hp, a_had);
@@ -522,7 +564,13 @@ using namespace exl3b;
 
 extern "C" size_t exl3b_linear_workspace_bytes(int m, int k, int groups, int64_t n_total) {
     if (m < 1 || k < 128 || groups < 1 || n_total < 128) return 0;
-    return ws_layout(m, k, groups, n_total).total;
+    // an upper bound over every K and every split of n_total into `groups` widths
+    const int64_t blocks = n_total / 128;
+    Partition q = {};
+    q.super_blocks = (int)std::min<int64_t>(blocks, (blocks + 7) / 8 + groups - 1);
+    q.sb_cols = (int)std::min<int64_t>(blocks, 8) * 128;
+    q.ctas = (int)std::min<int64_t>(num_sms(), (int64_t)q.super_blocks * ((k / 16) / rows_per_unit(8)));
+    return ws_layout(m, k, groups, q).total;
 }
 
 extern "C" int exl3b_linear(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K, int codebook,
