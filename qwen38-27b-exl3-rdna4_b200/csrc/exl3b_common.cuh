@@ -222,6 +222,10 @@ EXL3B_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }\n"
                  :: "r"(bar), "r"(bytes) : "memory");
 }
+// add expected transaction bytes to the current phase without arriving
+EXL3B_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;\n" :: "r"(bar), "r"(bytes) : "memory");
+}
 // try_wait with a suspend-time hint: a waiting warp sleeps in hardware (up to ~20 us per try)
 // instead of spinning through issue slots that the decoding warps need
 EXL3B_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {

@@ -1,12 +1,12 @@
 // The EXL3 linear for 1 <= m <= 16 rows (decode and speculative verify), fused end to end:
 //
-//   launch 1  had_in:  A_had = fp16(H128 * fp16(x * suh) / sqrt(128)) -> workspace, k-tile-major
-//                      [group][k/16][m][16 halves] with each 16-half row in mma B-fragment order
-//   launch 2  gemv:    stream-K over units of R trellis k-tile rows x one super-block of up to
+//   one launch:        stream-K over units of R trellis k-tile rows x one super-block of up to
 //                      1024 output columns (64 n-tiles).  In the checkpoint layout
 //                      [k/16][n/16][16K] a unit row is one contiguous run of up to 64 x 32K
-//                      bytes (8 KB at K = 4), so a producer warp fetches a unit with R + 1 bulk
-//                      copies (no multicast) into a shared-memory ring.  Sixteen decode warps
+//                      bytes (8 KB at K = 4), so a producer warp fetches a unit with R bulk
+//                      copies (no multicast) into a shared-memory ring, and while they fly it
+//                      writes the unit's input transform A_had = fp16(H128 fp16(x * suh) / sqrt(128))
+//                      next to them, in mma B-fragment order.  Sixteen decode warps
 //                      decode the trellis in registers straight into mma.m16n8k16 A fragments
 //                      (W^T x A_had^T, fp32 accumulate); warp w owns n-tiles w, w+16, w+32, w+48 of
 //                      the super-block.  When the CTA leaves a super-block the decode warps pool
@@ -14,7 +14,9 @@
 //                      it reduces the block across the CTAs that shared it (partials in the
 //                      workspace, fixed summation order, last arriver finishes) and applies
 //                      had_out + svh.
-//   Launch 2 is a programmatic dependent launch: its trellis copies start while launch 1 runs.
+//   The launch is a programmatic dependent launch: the first ring of trellis copies is issued
+//   before griddepcontrol.wait, so weight streaming overlaps the end of the previous kernel; x,
+//   the workspace and y are touched only after the wait.
 //
 // Reference semantics: reference/exl3_oracle.py:307-351 (gemv_mul1, all codebooks);
 // kernels replaced: exl3_gemm / exl3_gemv_mr / exl3_mgemm / exl3_gemv_mr_grouped of the fork
@@ -53,48 +55,17 @@ struct GemvGroups {
 
 struct GemvParams {
     GemvGroups g;
-    const __half* a_had;  // workspace
+    const __half* x;      // [m][k]
+    const __half* suh[EXL3B_MAX_GROUPS];
     float* partials;      // workspace: [ctas + super-blocks - 1][m][sb_cols], slot = cta + super-block
     int* counters;        // workspace: one per global column block
     int* err;             // workspace error word
-    int groups, m, kt;    // kt = k / 16
+    int groups, m, k, kt;  // kt = k / 16
     int ku;               // units per super-block = kt / R
     int units, ctas;
     int sb_cols;          // widest super-block of the call, in columns
     int64_t ldy;
 };
-
-struct HadInParams {
-    const __half* suh[EXL3B_MAX_GROUPS];
-};
-
-// ---------------------------------------------------------------------------------------------
-// launch 1: input transform, one warp per (row, k-block of 128, group)
-// ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) had_in_kernel(const __half* __restrict__ x, int m, int k,
-                                                     const __grid_constant__ HadInParams p,
-                                                     __half* __restrict__ a_had) {
-    griddep_launch();
-    const int row = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j = blockIdx.x, g = blockIdx.y;
-    if (row >= m) return;
-    const int c = j * 128 + 4 * lane;
-    const uint2 xr = *reinterpret_cast<const uint2*>(x + (int64_t)row * k + c);
-    const uint2 sr = *reinterpret_cast<const uint2*>(p.suh[g] + c);
-    const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
-    const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
-    float v[4] = {__low2float(p01), __high2float(p01), __low2float(p23), __high2float(p23)};
-    had128_warp(v);
-    const uint32_t h01 = h2_as_u32(__floats2half2_rn(v[0] * kRScale, v[1] * kRScale));
-    const uint32_t h23 = h2_as_u32(__floats2half2_rn(v[2] * kRScale, v[3] * kRScale));
-    // element e = 4*lane + s sits in k-tile 8j + e/16 at the fragment slot of kk = e%16:
-    // kk = 2q + b -> 4q + b (kk < 8);  kk = 8 + 2q + b -> 4q + 2 + b
-    const int kt = lane >> 2, kq = lane & 3;
-    const int base = (kq < 2) ? 8 * kq : 8 * (kq - 2) + 2;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(a_had + (((int64_t)g * (k / 16) + 8 * j + kt) * m + row) * 16);
-    dst[base >> 1] = h01;
-    dst[(base + 4) >> 1] = h23;
-}
 
 // ---------------------------------------------------------------------------------------------
 // stream-K partition helpers (64-bit: U * P fits easily)
@@ -166,45 +137,90 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     }
     __syncthreads();
 
+    griddep_launch();  // the next kernel in the stream may start its own prologue
+
     if (warp == kProducerWarp) {
         // ------------------------------ producer warp ------------------------------
-        bool waited_dep = false;
-        int issued = 0;
+        // issue(i): claim unit i's stage (after the decode warps released it), announce its bytes
+        // and start its R trellis row copies.  transform(i): write its A_had rows, then arrive.
         int sb = -1;
         SbInfo si = {0, 0, 0};
-        for (int i = 0; i < nunits; ++i) {
-            const int s = i % kStages, n = i / kStages;
-            bool ok = true;
-            if (n > 0) ok = mbar_wait(empty0 + 8 * s, (n - 1) & 1, p.err, 1);
-            if (!ok) *abort_flag = 1;
-            if (__any_sync(0xFFFFFFFFu, *abort_flag != 0)) break;
-            const int u = u0 + i;
+        int issued = 0;
+        auto locate = [&](int u) {
             if (u / ku != sb) {
                 sb = u / ku;
                 si = sb_info(p.g, p.groups, sb);
             }
+        };
+        auto issue = [&](int i) -> bool {
+            const int s = i % kStages, n = i / kStages;
+            if (n > 0) {
+                const bool ok = mbar_wait_or_abort(empty0 + 8 * s, (n - 1) & 1, p.err, 1, abort_flag);
+                if (!__all_sync(0xFFFFFFFFu, ok)) return false;
+            }
+            const int u = u0 + i;
+            locate(u);
             const int kr0 = (u - sb * ku) * R;
             const uint32_t row_bytes = (uint32_t)si.nblk * 8 * S::kTile;
-            const uint32_t ahad_bytes = (uint32_t)(R * m * 32);
-            const uint32_t st = sbase + s * S::kStageBytes;
-            if (lane == 0) mbar_arrive_expect_tx(full0 + 8 * s, R * row_bytes + ahad_bytes);
+            if (lane == 0) mbar_expect_tx(full0 + 8 * s, R * row_bytes);
             __syncwarp();
             if (lane < R) {
                 const uint16_t* src =
                     p.g.trellis[si.g] + ((int64_t)(kr0 + lane) * p.g.n_tiles[si.g] + si.b0 * 8) * (16 * K);
-                bulk_g2s(st + lane * S::kRowBytes, src, row_bytes, full0 + 8 * s);
-            } else if (lane == R) {
-                if (!waited_dep) { griddep_wait(); waited_dep = true; }
-                const __half* src = p.a_had + ((int64_t)si.g * p.kt + kr0) * m * 16;
-                bulk_g2s(st + S::kTrellisStage, src, ahad_bytes, full0 + 8 * s);
+                bulk_g2s(sbase + s * S::kStageBytes + lane * S::kRowBytes, src, row_bytes, full0 + 8 * s);
             }
             issued = i + 1;
+            return true;
+        };
+        // A_had of the unit's R k-tiles (inside one 128-input block) for rows 0..m-1, as
+        // fp16(H128 fp16(x * suh) / sqrt(128)); lane l transforms inputs 4l..4l+3 of the block,
+        // which sit in k-tile l/4 at fragment slots kk = 2q + b -> 4q + b, 8 + 2q + b -> 4q + 2 + b
+        const int ktl = lane >> 2, kq = lane & 3;
+        const int slot = (kq < 2) ? 8 * kq : 8 * (kq - 2) + 2;
+        auto transform = [&](int i) {
+            const int u = u0 + i;
+            locate(u);
+            const int kr0 = (u - sb * ku) * R;
+            const int blk = kr0 >> 3, t0 = kr0 & 7;
+            const int col = blk * 128 + 4 * lane;
+            const uint2 sr = *reinterpret_cast<const uint2*>(p.suh[si.g] + col);
+            const bool mine = ktl >= t0 && ktl < t0 + R;
+            uint32_t* dst = reinterpret_cast<uint32_t*>(smem + (i % kStages) * S::kStageBytes + S::kTrellisStage +
+                                                        (ktl - t0) * m * 32) + (slot >> 1);
+            for (int row = 0; row < m; ++row) {
+                const uint2 xr = *reinterpret_cast<const uint2*>(p.x + (int64_t)row * p.k + col);
+                const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
+                const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
+                float v[4] = {__low2float(p01), __high2float(p01), __low2float(p23), __high2float(p23)};
+                had128_warp(v);
+                if (mine) {
+                    dst[row * 8] = h2_as_u32(__floats2half2_rn(v[0] * kRScale, v[1] * kRScale));
+                    dst[row * 8 + 2] = h2_as_u32(__floats2half2_rn(v[2] * kRScale, v[3] * kRScale));
+                }
+            }
+        };
+        bool live = true;
+        int published = 0;
+        for (int i = 0; live && i < min(nunits, kStages); ++i) live = issue(i);
+        griddep_wait();  // x may come from the previous kernel
+        for (int i = 0; live && i < nunits; ++i) {
+            if (i >= kStages) live = issue(i);
+            if (!live) break;
+            transform(i);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full0 + 8 * (i % kStages));
+            published = i + 1;
         }
-        // No copy may still be landing in shared memory when the CTA exits: wait (bounded) for
-        // the last fill of every stage.  Normally these completed long ago.
-        if (lane == 0)
+        // No copy may still be landing in shared memory when the CTA exits: after an abort, arrive
+        // on the stages whose copies were issued but never published (their phase then completes
+        // with the copies), and wait (bounded) for the last fill of every stage.  Normally these
+        // completed long ago.
+        if (lane == 0) {
+            if (!live) *abort_flag = 1;
+            for (int i = published; i < issued; ++i) mbar_arrive(full0 + 8 * (i % kStages));
             for (int i = max(0, issued - kStages); i < issued; ++i)
                 mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1, p.err, 2);
+        }
         return;
     }
 
@@ -281,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         if (!sb_end) continue;
 
         // ---------------- pool the finished super-block, then one warp per column block ----------------
+        griddep_wait();  // the workspace counters and y may still belong to the previous kernel
         named_bar(kFlushBar, kDecodeWarps * 32);  // the previous flush's readers are done with acc_s
         // fragment -> acc_s[row][col]: lane (gq, tq) holds D[col gq (+8)][rows 2tq, 2tq+1] of n-tile
         // warp + 16 j
@@ -436,14 +453,13 @@ static Partition partition(int k, int K, int groups, const int* n) {
 }
 
 struct WsLayout {
-    size_t counters, a_had, partials, total;
+    size_t counters, partials, total;
 };
 
 static WsLayout ws_layout(int m, int k, int groups, const Partition& q) {
     WsLayout L;
     L.counters = kHeaderBytes;
-    L.a_had = round_up(L.counters + kCounterBytes, 256);
-    L.partials = round_up(L.a_had + (size_t)groups * (k / 16) * m * 32, 256);
+    L.partials = round_up(L.counters + kCounterBytes, 256);
     L.total = round_up(L.partials + (size_t)(q.ctas + q.super_blocks - 1) * m * q.sb_cols * 4, 256);
     return L;
 }
@@ -511,13 +527,11 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
 
     cudaStream_t st = (cudaStream_t)stream;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    __half* a_had = reinterpret_cast<__half*>(ws + L.a_had);
 
-    HadInParams hp = {};
     GemvParams p = {};
     int blk = 0, sbs = 0;
     for (int g = 0; g < groups; ++g) {
-        hp.suh[g] = reinterpret_cast<const __half*>(suh[g]);
+        p.suh[g] = reinterpret_cast<const __half*>(suh[g]);
         p.g.trellis[g] = trellis[g];
         p.g.svh[g] = reinterpret_cast<const __half*>(svh[g]);
         p.g.y[g] = reinterpret_cast<__half*>(y[g]);
@@ -533,12 +547,13 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     }
     p.g.blk_prefix[groups] = blk;
     p.g.sb_prefix[groups] = sbs;
-    p.a_had = a_had;
+    p.x = reinterpret_cast<const __half*>(x);
     p.partials = reinterpret_cast<float*>(ws + L.partials);
     p.counters = reinterpret_cast<int*>(ws + L.counters);
     p.err = reinterpret_cast<int*>(ws);
     p.groups = groups;
     p.m = m;
+    p.k = k;
     p.kt = k / 16;
     p.ku = q.ku;
     p.units = q.units;
@@ -546,9 +561,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     p.sb_cols = q.sb_cols;
     p.ldy = ldy;
 
-    had_in_kernel<<<dim3(k / 128, groups), dim3(32 * m), 0, st>>>(reinterpret_cast<const __half*>(x), m, k, hp, a_had);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e);
+    cudaError_t e;
     const bool mt2 = m > 8;
     switch (codebook) {
         case 0: e = mt2 ? launch_gemv_k<0, 2>(K, p, st) : launch_gemv_k<0, 1>(K, p, st); break;

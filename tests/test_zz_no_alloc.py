@@ -69,12 +69,21 @@ def test_noalloc_matches_regular_entry_point(lib, m, k, n, K, cb):
 
 
 def test_noalloc_rejects_calls_beyond_its_scratch(lib):
-    k, n = 1 << 20, 128  # A_had alone would need 32 MiB at m = 16
-    x = torch.zeros(16, 128, dtype=torch.float16, device=DEV)  # never read: rejected before launch
-    y = torch.full((16, n), float("nan"), dtype=torch.float16, device=DEV)
-    st = lib.lib().exl3b_linear_noalloc(x.data_ptr(), 16, k, x.data_ptr(), n, 4, 2, x.data_ptr(), x.data_ptr(),
-                                        y.data_ptr(), n, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    # n = 2^20 columns at m = 16: the cross-CTA partial sums alone need far more than the static
+    # scratch.  Every buffer has the size the call declares, so nothing could be read out of bounds
+    # even if the call were accepted.
+    m, k, n, K = 16, 128, 1 << 20, 4
+    L = lib.lib()
+    need = L.exl3b_linear_workspace_bytes(m, k, 1, n)
+    assert need > 8 << 20, need
+    x = torch.zeros(m, k, dtype=torch.float16, device=DEV)
+    tr = torch.zeros(k // 16, n // 16, 16 * K, dtype=torch.int16, device=DEV)
+    suh = torch.ones(k, dtype=torch.float16, device=DEV)
+    svh = torch.ones(n, dtype=torch.float16, device=DEV)
+    y = torch.full((m, n), float("nan"), dtype=torch.float16, device=DEV)
+    st = L.exl3b_linear_noalloc(x.data_ptr(), m, k, tr.data_ptr(), n, K, 2, suh.data_ptr(), svh.data_ptr(),
+                                y.data_ptr(), n, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     assert st == lib.EXL3B_TOO_LARGE
-    assert b"static scratch" in lib.lib().exl3b_status_string(st)
+    assert b"static scratch" in L.exl3b_status_string(st)
     assert torch.isnan(y).all()
