@@ -185,9 +185,10 @@ def _cpu_slice(args):
     return time.perf_counter() - t0
 
 
-def cpu_baseline(K: int, budget_cols: int = 17408) -> dict:
-    """Time the oracle's linear (M=1, mul1) on a column sample of the gate layer, one slice per
-    host core in a spawn pool; report the metric's unit for that sample."""
+def cpu_baseline(K: int, budget_cols: int = 131072) -> dict:
+    """Time the oracle's linear (M=1, mul1) on a column sample of gate_proj-shaped weights (k = 5120),
+    one slice per host core in a spawn pool, about ten seconds of host work in all; report the
+    metric's unit for that sample."""
     import multiprocessing as mp
     cores = os.cpu_count() or 1
     per = max(128, (budget_cols // cores) // 128 * 128)
@@ -463,6 +464,9 @@ def main():
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = gu_bytes / (gu_ms_med * 1e-3) / 1e9
+    # DRAM bytes (read + write) of one gemv_kernel launch of this call, from the ncu capture
+    # summarised in profiles/gemv_kernel_gate_up_m1_k4.md (measured for K = 4, m = 1 only)
+    traffic = (89.291264e6 + 3.387904e6) if (K == 4 and M == 1 and world == 1) else None
 
     # ---- end to end: pinned host x -> device, the layer's ops (graph), y -> pinned host ----
     x_host = torch.randn((M, HIDDEN), dtype=torch.float32).to(torch.bfloat16).pin_memory()
@@ -509,14 +513,16 @@ def main():
         "data": "synthetic (seeded uniform trellis codes, +-1 signs, x ~ N(0,1) bf16)", "config": config,
         "step_ms_median": statistics.median(step_ms),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": None,
-                     "kernel": "gate_up linear_groups call (had_in + gemv_kernel, graph-replayed), median "
+                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "kernel": "gate_up linear_groups call (gemv_kernel, graph-replayed), median "
                                f"of {n_calls} event-timed calls, {gu_bytes} algorithmic bytes per call",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel "
+                                       "launch (profiles/gemv_kernel_gate_up_m1_k4.md)" if traffic else None,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650"},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 2),
                 "d2h_bytes_per_step": int(y_host.numel() * 2)},
-        "gpu_launches": args.steps * 2 * len(MODULES),
+        "gpu_launches": args.steps * len(MODULES),
         "clocks": clocks,
         **extra,
     }
