@@ -185,7 +185,7 @@ def _cpu_slice(args):
     return time.perf_counter() - t0
 
 
-def cpu_baseline(K: int, budget_cols: int = 131072) -> dict:
+def cpu_baseline(K: int, budget_cols: int = 524288) -> dict:
     """Time the oracle's linear (M=1, mul1) on a column sample of gate_proj-shaped weights (k = 5120),
     one slice per host core in a spawn pool, about ten seconds of host work in all; report the
     metric's unit for that sample."""
