@@ -136,9 +136,11 @@ def make_layer(torch, dev, K, tp, rank, seed):
     return out
 
 
-def run_layer(torch, layer, x, inputs, K, tp, pg):
+def run_layer(torch, layer, x, inputs, K, tp, pg, comm=None):
     """One decoder layer's EXL3 linears as the engine calls them: x feeds qkv and gate_up; the
-    row-parallel o and down read their own (sharded) inputs.  Returns the last output."""
+    row-parallel o and down read their own (sharded) inputs.  Under tensor parallelism o and down
+    reduce across ranks inside their kernel (comm), or with an NCCL all-reduce after it (no comm).
+    Returns the last output."""
     ops = torch.ops.exl3rocm
     y = None
     for mod, names in MODULES:
@@ -147,6 +149,10 @@ def run_layer(torch, layer, x, inputs, K, tp, pg):
         sv = [layer[nm][2] for nm in names]
         kin = layer[names[0]][3]
         xin = x if kin == x.shape[1] and mod in ("qkv", "gate_up") else inputs[kin]
+        if tp > 1 and mod in ("o", "down") and comm is not None:
+            from exl3rocm.tp import linear_tp
+            y = linear_tp(xin, ts[0], su[0], sv[0], K, False, True, comm)
+            continue
         if len(names) == 1:
             y = ops.linear(xin, ts[0], su[0], sv[0], K, False, True)
         else:
@@ -322,6 +328,9 @@ def main():
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the KV-attention and prefill legs")
+    ap.add_argument("--tp-reduce", default="fused", choices=["fused", "nccl"],
+                    help="row-parallel reduction under --gpus > 1: inside the GEMV kernel over peer memory, "
+                         "or an NCCL all-reduce after it")
     ap.add_argument("--modules", default="qkv,o,gate_up,down",
                     help="comma list of the layer's modules a step runs (default: all four)")
     args = ap.parse_args()
@@ -339,7 +348,8 @@ def main():
     config = {"workload": f"one 27B-class decoder layer's EXL3 linears ({','.join(m_ for m_, _ in MODULES)}), M={M}, "
                           f"{K} bits, mul1 codebook, x bf16 cast to fp16", "model": "synthetic 27B-class layer",
               "hidden": HIDDEN, "intermediate": INTER, "m": M, "bits": K, "tp": world,
-              "parallelism": f"tp{world}" if world > 1 else "single", "l2": "weights rotate over copies > 2x L2"}
+              "parallelism": f"tp{world}" if world > 1 else "single",
+              "tp_reduce": (args.tp_reduce if world > 1 else None), "l2": "weights rotate over copies > 2x L2"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -369,6 +379,10 @@ def main():
         pg = torch.distributed.group.WORLD
     import exl3rocm.ops  # noqa: F401  registers torch.ops.exl3rocm.*
     from exl3rocm import ops as xops
+    comm = None
+    if world > 1 and args.tp_reduce == "fused":
+        from exl3rocm.tp import TpComm
+        comm = TpComm(pg, dev, max_blocks=HIDDEN // 128)
 
     one = layer_bytes(K, M, 1) // 1
     copies = max(2, int(np.ceil(3 * L2_BYTES * world / max(1, one))))  # per-rank bytes > 3x L2
@@ -389,12 +403,12 @@ def main():
             for mod, names in MODULES:
                 xops.reserve_workspace(dev, lay[names[0]][3], sum(lay[nm][4] for nm in names), len(names), 16)
         for i in range(3):
-            run_layer(torch, layers[i % copies], x, inputs, K, world, pg)
+            run_layer(torch, layers[i % copies], x, inputs, K, world, pg, comm)
         stream.synchronize()
         for lay in layers:
             g_ = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g_, stream=stream):
-                outs.append(run_layer(torch, lay, x, inputs, K, world, pg))
+                outs.append(run_layer(torch, lay, x, inputs, K, world, pg, comm))
             graphs.append(g_)
         # gate_up alone, for the per-call roofline of the dominant kernel
         gu_graphs = []
@@ -503,6 +517,8 @@ def main():
 
     if world > 1:
         torch.distributed.barrier(device_ids=[local])
+        if comm is not None:
+            comm.close()
         torch.distributed.destroy_process_group()
     if rank != 0:
         return

@@ -188,6 +188,41 @@ EXL3B_API int exl3b_linear_noalloc(const uint16_t* x, int m, int k, const uint16
                                    int codebook, const uint16_t* suh, const uint16_t* svh, uint16_t* y,
                                    int64_t ldy, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Tensor-parallel row-parallel linear with the all-reduce fused into the kernel.  The reference
+ * runs no tensor parallelism (vllm_plugin/exl3rocm/plugin.py:255-257 raises); under vLLM this
+ * replaces exl3_gemm on an o_proj / down_proj shard followed by RowParallelLinear's all-reduce.
+ *
+ * Every rank owns one communication buffer of exl3b_tp_comm_bytes(tp_size, max_blocks, max_rows)
+ * bytes, zeroed once, and maps every peer's buffer with CUDA IPC (exl3b_ipc_get_handle /
+ * exl3b_ipc_open_handle).  exl3b_linear_tp computes this rank's k-slice of the product, exchanges
+ * the fp32 partial sums of each 128-column block with all ranks through the peers' buffers (plain
+ * peer stores over NVLink, a flag per block and call, bounded waits), and writes the full output
+ * y = had_out(fp16(sum over ranks), svh) on every rank: no further all-reduce is needed.  All ranks
+ * must make the same sequence of calls on a buffer, and the calls of one rank on one buffer must
+ * be stream-ordered.  Waits that give up after about a second set the workspace error word. */
+#define EXL3B_MAX_TP 8
+typedef struct {
+    int tp_size;                      /* 2 .. EXL3B_MAX_TP */
+    int tp_rank;
+    int max_blocks;                   /* the buffers hold up to max_blocks 128-column blocks */
+    int max_rows;                     /* ... of up to max_rows rows (<= EXL3B_GEMV_MAX_ROWS) */
+    void* buffers[EXL3B_MAX_TP];      /* every rank's buffer, mapped into this process (own included) */
+} exl3b_tp_comm;
+
+EXL3B_API size_t exl3b_tp_comm_bytes(int tp_size, int max_blocks, int max_rows);
+/* A CUDA IPC handle of the allocation holding dev_ptr plus dev_ptr's offset inside it
+ * (EXL3B_IPC_HANDLE_BYTES bytes), and the pointer it names, mapped into another process. */
+#define EXL3B_IPC_HANDLE_BYTES 72
+EXL3B_API int exl3b_ipc_get_handle(const void* dev_ptr, void* handle);
+EXL3B_API int exl3b_ipc_open_handle(const void* handle, void** dev_ptr);
+EXL3B_API int exl3b_ipc_close(void* dev_ptr);
+/* x holds this rank's k/tp_size input features (k here is that local width), trellis / suh its
+ * k-slice; n is the full output width (n / 128 <= comm->max_blocks, m <= comm->max_rows). */
+EXL3B_API int exl3b_linear_tp(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K, int codebook,
+                              const uint16_t* suh, const uint16_t* svh, uint16_t* y, int64_t ldy,
+                              void* workspace, size_t workspace_bytes, const exl3b_tp_comm* comm, void* stream);
+
 /* Reads the kernel error word of a linear workspace (0 = none; otherwise the code of a wait that
  * gave up) into *out, synchronising `stream`.  Test and diagnostics helper. */
 EXL3B_API int exl3b_linear_workspace_error(const void* workspace, int* out, void* stream);

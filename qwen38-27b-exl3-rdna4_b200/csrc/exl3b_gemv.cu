@@ -24,6 +24,7 @@
 // every row equals the m = 1 result bit for bit: here the work partition depends only on
 // (k, n, groups, K) and each mma column is one input row, so rows never interact).
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -35,7 +36,7 @@ constexpr int kDecodeWarps = 16;
 constexpr int kProducerWarp = kDecodeWarps;
 constexpr int kThreads = (kDecodeWarps + 1) * 32;
 constexpr int kFlushBar = 1;      // named barrier of the decode warps
-constexpr int kMaxBatch = 8;      // partials a finishing warp loads before summing them
+constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summing them
 constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
 constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
 
@@ -65,7 +66,30 @@ struct GemvParams {
     int units, ctas;
     int sb_cols;          // widest super-block of the call, in columns
     int64_t ldy;
+    // fused tensor-parallel all-reduce (tp_size > 1): every rank's communication buffer
+    int tp_size, tp_rank, tp_blocks, tp_rows;
+    uint8_t* tp_buf[EXL3B_MAX_TP];
 };
+
+// Communication buffer of one rank: a 256-byte header (call counter, finished-CTA counter), flags
+// [2 parities][tp ranks][blocks] int32, then data [2][tp][blocks][rows][128] fp32.  Rank s writes
+// its partial of block b for call e into every rank's slot [e & 1][s][b] and then the flag, set to e.
+constexpr size_t kTpHeader = 256;
+__host__ __device__ inline size_t tp_flag_bytes(int tp, int blocks) {
+    return ((size_t)2 * tp * blocks * 4 + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t tp_comm_bytes(int tp, int blocks, int rows) {
+    return kTpHeader + tp_flag_bytes(tp, blocks) + (size_t)2 * tp * blocks * rows * 128 * 4;
+}
+
+EXL3B_DEV void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;\n" :: "l"(p), "r"(v) : "memory");
+}
+EXL3B_DEV int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // ---------------------------------------------------------------------------------------------
 // stream-K partition helpers (64-bit: U * P fits easily)
@@ -111,6 +135,138 @@ struct GemvSmem {
     static constexpr int kFlagOffset = kBarOffset + 2 * kStages * 8;
     static constexpr int kTotal = kFlagOffset + 16;
 };
+
+// One decode warp finishes column block `blk` of super-block `sb` (only when a CTA leaves a
+// super-block).
+template <int MT>
+__device__ __forceinline__ void flush_block(const GemvParams& p, const float* acc_s, volatile int* abort_flag, int c,
+                                         int sb, SbInfo si, int blk, int u0, int u1, int lane) {
+    const int ku = p.ku, U = p.units, P = p.ctas, m = p.m;
+    // If this CTA covered the super-block's whole k range, transform and store; otherwise
+    // publish the partial and, if it is the last of the block's CTAs to arrive, gather all
+    // partials in fixed CTA order and finish the block.
+    const int seg_lo = max(u0, sb * ku), seg_hi = min(u1, (sb + 1) * ku);
+    const bool whole = (seg_lo == sb * ku) && (seg_hi == (sb + 1) * ku);
+    const int cf = cta_of_unit(sb * ku, U, P), cl = cta_of_unit((sb + 1) * ku - 1, U, P);
+    const int Bg = p.g.blk_prefix[si.g] + si.b0 + blk;
+    const int col = blk * 128 + 4 * lane;  // column inside the super-block
+    bool finalize = whole;
+    if (!whole) {
+        // CTA ranges are contiguous and ordered, so cta + super-block is unique among the
+        // (CTA, super-block) pairs that meet
+        float* mine = p.partials + ((int64_t)(c + sb) * m) * p.sb_cols;
+        for (int row = 0; row < m; ++row)
+            __stcg(reinterpret_cast<float4*>(mine + (int64_t)row * p.sb_cols + col),
+                   *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col));
+        __syncwarp();
+        int v = 0;
+        if (lane == 0) {
+            // cumulative fence over the warp's partial stores, then the counter; the
+            // second fence orders the reads of other CTAs' partials after it
+            __threadfence();
+            v = atomicAdd(p.counters + Bg, 1);
+            __threadfence();
+        }
+        v = __shfl_sync(0xFFFFFFFFu, v, 0);
+        finalize = (v == cl - cf);
+    }
+    if (finalize) {
+        const int b = si.b0 + blk;
+        const uint2 sv = *reinterpret_cast<const uint2*>(p.g.svh[si.g] + b * 128 + 4 * lane);
+        // this CTA's k-range partial of the block, summed over the CTAs that shared it
+        auto block_sum = [&](int row, float (&v)[4]) {
+            v[0] = v[1] = v[2] = v[3] = 0.f;
+            for (int c0 = cf; c0 <= cl; c0 += kMaxBatch) {
+                // all loads of a batch in flight together, then summed in CTA order
+                float4 t[kMaxBatch];
+#pragma unroll
+                for (int q = 0; q < kMaxBatch; ++q) {
+                    const int cc = c0 + q;
+                    if (cc > cl) break;
+                    t[q] = (cc == c) ? *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col)
+                                     : __ldcg(reinterpret_cast<const float4*>(
+                                           p.partials + ((int64_t)(cc + sb) * m + row) * p.sb_cols + col));
+                }
+#pragma unroll
+                for (int q = 0; q < kMaxBatch; ++q) {
+                    if (c0 + q > cl) break;
+                    v[0] += t[q].x; v[1] += t[q].y; v[2] += t[q].z; v[3] += t[q].w;
+                }
+            }
+        };
+        // c_rot is stored fp16 between the dot and the output transform (oracle :349-351)
+        auto finish_row = [&](int row, const float (&v)[4]) {
+            const __half2 c01 = __floats2half2_rn(v[0], v[1]), c23 = __floats2half2_rn(v[2], v[3]);
+            float h[4] = {__low2float(c01), __high2float(c01), __low2float(c23), __high2float(c23)};
+            had128_warp(h);
+            __half2 y01 = __floats2half2_rn(h[0] * kRScale, h[1] * kRScale);
+            __half2 y23 = __floats2half2_rn(h[2] * kRScale, h[3] * kRScale);
+            y01 = __hmul2(y01, u32_as_h2(sv.x));
+            y23 = __hmul2(y23, u32_as_h2(sv.y));
+            *reinterpret_cast<uint2*>(p.g.y[si.g] + row * p.ldy + b * 128 + 4 * lane) =
+                make_uint2(h2_as_u32(y01), h2_as_u32(y23));
+        };
+        if (p.tp_size <= 1) {
+            for (int row = 0; row < m; ++row) {
+                float v[4];
+                block_sum(row, v);
+                finish_row(row, v);
+            }
+        } else {
+            // Exchange this rank's k-slice partial of block b with every rank: data into
+            // slot [par][rank][b] of each rank's buffer, a system fence, then the flags;
+            // wait for every rank's flag of this call in our own buffer, sum in rank order.
+            const int tp = p.tp_size, rk = p.tp_rank, nb = p.tp_blocks, rows = p.tp_rows;
+            const int ep = ld_acquire_sys(reinterpret_cast<const int*>(p.tp_buf[rk])) + 1;
+            const int par = ep & 1;
+            const size_t fbytes = tp_flag_bytes(tp, nb);
+            for (int row = 0; row < m; ++row) {
+                float v[4];
+                block_sum(row, v);
+                for (int r = 0; r < tp; ++r) {
+                    float* d = reinterpret_cast<float*>(p.tp_buf[r] + kTpHeader + fbytes) +
+                               ((((int64_t)par * tp + rk) * nb + b) * rows + row) * 128 + 4 * lane;
+                    __stcg(reinterpret_cast<float4*>(d), make_float4(v[0], v[1], v[2], v[3]));
+                }
+            }
+            __threadfence_system();
+            __syncwarp();
+            if (lane < tp)
+                st_release_sys(reinterpret_cast<int*>(p.tp_buf[lane] + kTpHeader) + ((int64_t)par * tp + rk) * nb + b, ep);
+            bool ok = true;
+            if (lane < tp) {
+                const int* f = reinterpret_cast<const int*>(p.tp_buf[rk] + kTpHeader) + ((int64_t)par * tp + lane) * nb + b;
+                if (ld_acquire_sys(f) != ep) {
+                    const long long t0 = clock64();
+                    while (ld_acquire_sys(f) != ep) {
+                        if (clock64() - t0 > kWaitCycles) { ok = false; break; }
+                        __nanosleep(64);
+                    }
+                }
+            }
+            if (!__all_sync(0xFFFFFFFFu, ok)) {
+                if (lane == 0) { atomicExch(p.err, 6); *abort_flag = 1; }
+            } else {
+                // every lane acquires every flag itself, so that its own loads of the partials below
+                // are ordered after the peers' release stores
+                for (int r = 0; r < tp; ++r)
+                    (void)ld_acquire_sys(reinterpret_cast<const int*>(p.tp_buf[rk] + kTpHeader) +
+                                         ((int64_t)par * tp + r) * nb + b);
+                const float* mine = reinterpret_cast<const float*>(p.tp_buf[rk] + kTpHeader + fbytes);
+                for (int row = 0; row < m; ++row) {
+                    float v[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int r = 0; r < tp; ++r) {  // fixed rank order: identical sums on every rank
+                        const float4 t = __ldcg(reinterpret_cast<const float4*>(
+                            mine + ((((int64_t)par * tp + r) * nb + b) * rows + row) * 128 + 4 * lane));
+                        v[0] += t.x; v[1] += t.y; v[2] += t.z; v[3] += t.w;
+                    }
+                    finish_row(row, v);
+                }
+            }
+        }
+        if (!whole && lane == 0) p.counters[Bg] = 0;
+    }
+}
 
 template <int K, int CB, int MT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
@@ -321,77 +477,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                 for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
             }
         named_bar(kFlushBar, kDecodeWarps * 32);
-        if (warp < si.nblk && *abort_flag == 0) {
-            // If this CTA covered the super-block's whole k range, transform and store; otherwise
-            // publish the partial and, if it is the last of the block's CTAs to arrive, gather all
-            // partials in fixed CTA order and finish the block.
-            const int blk = warp;
-            const int seg_lo = max(u0, sb * ku), seg_hi = min(u1, (sb + 1) * ku);
-            const bool whole = (seg_lo == sb * ku) && (seg_hi == (sb + 1) * ku);
-            const int cf = cta_of_unit(sb * ku, U, P), cl = cta_of_unit((sb + 1) * ku - 1, U, P);
-            const int Bg = p.g.blk_prefix[si.g] + si.b0 + blk;
-            const int col = blk * 128 + 4 * lane;  // column inside the super-block
-            bool finalize = whole;
-            if (!whole) {
-                // CTA ranges are contiguous and ordered, so cta + super-block is unique among the
-                // (CTA, super-block) pairs that meet
-                float* mine = p.partials + ((int64_t)(c + sb) * m) * p.sb_cols;
-                for (int row = 0; row < m; ++row)
-                    __stcg(reinterpret_cast<float4*>(mine + (int64_t)row * p.sb_cols + col),
-                           *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col));
-                __syncwarp();
-                int v = 0;
-                if (lane == 0) {
-                    // cumulative fence over the warp's partial stores, then the counter; the
-                    // second fence orders the reads of other CTAs' partials after it
-                    __threadfence();
-                    v = atomicAdd(p.counters + Bg, 1);
-                    __threadfence();
-                }
-                v = __shfl_sync(0xFFFFFFFFu, v, 0);
-                finalize = (v == cl - cf);
-            }
-            if (finalize) {
-                const int b = si.b0 + blk;
-                const uint2 sv = *reinterpret_cast<const uint2*>(p.g.svh[si.g] + b * 128 + 4 * lane);
-                for (int row = 0; row < m; ++row) {
-                    float v[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int c0 = cf; c0 <= cl; c0 += kMaxBatch) {
-                        // all loads of a batch in flight together, then summed in CTA order
-                        float4 t[kMaxBatch];
-#pragma unroll
-                        for (int q = 0; q < kMaxBatch; ++q) {
-                            const int cc = c0 + q;
-                            if (cc > cl) break;
-                            t[q] = (cc == c) ? *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col)
-                                             : __ldcg(reinterpret_cast<const float4*>(
-                                                   p.partials + ((int64_t)(cc + sb) * m + row) * p.sb_cols + col));
-                        }
-#pragma unroll
-                        for (int q = 0; q < kMaxBatch; ++q) {
-                            if (c0 + q > cl) break;
-                            v[0] += t[q].x; v[1] += t[q].y; v[2] += t[q].z; v[3] += t[q].w;
-                        }
-                    }
-                    // c_rot is stored fp16 between the dot and the output transform (oracle :349-351)
-                    const __half2 c01 = __floats2half2_rn(v[0], v[1]), c23 = __floats2half2_rn(v[2], v[3]);
-                    float h[4] = {__low2float(c01), __high2float(c01), __low2float(c23), __high2float(c23)};
-                    had128_warp(h);
-                    __half2 y01 = __floats2half2_rn(h[0] * kRScale, h[1] * kRScale);
-                    __half2 y23 = __floats2half2_rn(h[2] * kRScale, h[3] * kRScale);
-                    y01 = __hmul2(y01, u32_as_h2(sv.x));
-                    y23 = __hmul2(y23, u32_as_h2(sv.y));
-                    *reinterpret_cast<uint2*>(p.g.y[si.g] + row * p.ldy + b * 128 + 4 * lane) =
-                        make_uint2(h2_as_u32(y01), h2_as_u32(y23));
-                }
-                if (!whole && lane == 0) p.counters[Bg] = 0;
-            }
-        }
+        if (warp < si.nblk && *abort_flag == 0)
+            flush_block<MT>(p, acc_s, abort_flag, c, sb, si, warp, u0, u1, lane);
         if (i + 1 < nunits) {
             ++sb;
             si = sb_info(p.g, p.groups, sb);
             nj = 0;
             while (nj < 4 && warp + 16 * nj < si.nblk * 8) ++nj;
+        }
+    }
+    if (p.tp_size > 1) {
+        // the last CTA of the grid to get here advances this rank's call counter: every CTA read
+        // it (in its flushes) before arriving, and the next call reads it after griddepcontrol.wait
+        named_bar(kFlushBar, kDecodeWarps * 32);
+        if (threadIdx.x == 0) {
+            int* hdr = reinterpret_cast<int*>(p.tp_buf[p.tp_rank]);
+            __threadfence();
+            if (atomicAdd(hdr + 1, 1) == P - 1) {
+                hdr[1] = 0;
+                __threadfence();
+                atomicAdd(hdr, 1);
+            }
         }
     }
 }
@@ -504,8 +610,8 @@ static cudaError_t launch_gemv_k(int K, const GemvParams& p, cudaStream_t st) {
 }
 
 int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis, const int* n,
-                       int K, int codebook, const uint16_t* const* suh, const uint16_t* const* svh,
-                       uint16_t* const* y, int64_t ldy, void* workspace, size_t ws_bytes, void* stream) {
+                int K, int codebook, const uint16_t* const* suh, const uint16_t* const* svh, uint16_t* const* y,
+                int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm) {
     if (K < 1 || K > 8 || codebook < 0 || codebook > 2) return EXL3B_DECLINED;
     if (m < 1 || m > EXL3B_GEMV_MAX_ROWS || groups < 1 || groups > EXL3B_MAX_GROUPS) return EXL3B_DECLINED;
     if (k <= 0 || k % 128) return EXL3B_DECLINED;
@@ -521,6 +627,13 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
         n_total += n[g];
     }
     if (n_total / 128 > kMaxBlocks) return EXL3B_DECLINED;
+    if (comm) {
+        if (groups != 1 || comm->tp_size < 2 || comm->tp_size > EXL3B_MAX_TP || comm->tp_rank < 0 ||
+            comm->tp_rank >= comm->tp_size || n[0] / 128 > comm->max_blocks || m > comm->max_rows)
+            return EXL3B_BAD_ARG;
+        for (int r = 0; r < comm->tp_size; ++r)
+            if (!comm->buffers[r] || !aligned(comm->buffers[r], 256)) return EXL3B_BAD_ARG;
+    }
     const Partition q = partition(k, K, groups, n);
     const WsLayout L = ws_layout(m, k, groups, q);
     if (ws_bytes < L.total) return EXL3B_WORKSPACE;
@@ -560,6 +673,13 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     p.ctas = q.ctas;
     p.sb_cols = q.sb_cols;
     p.ldy = ldy;
+    p.tp_size = comm ? comm->tp_size : 1;
+    if (comm) {
+        p.tp_rank = comm->tp_rank;
+        p.tp_blocks = comm->max_blocks;
+        p.tp_rows = comm->max_rows;
+        for (int r = 0; r < comm->tp_size; ++r) p.tp_buf[r] = static_cast<uint8_t*>(comm->buffers[r]);
+    }
 
     cudaError_t e;
     const bool mt2 = m > 8;
@@ -594,7 +714,7 @@ extern "C" int exl3b_linear(const uint16_t* x, int m, int k, const uint16_t* tre
     const uint16_t* sv[1] = {svh};
     uint16_t* yy[1] = {y};
     int nn[1] = {n};
-    return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, workspace, workspace_bytes, stream);
+    return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, workspace, workspace_bytes, stream, nullptr);
 }
 
 extern "C" int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis,
@@ -602,7 +722,77 @@ extern "C" int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups,
                                     const uint16_t* const* svh, uint16_t* const* y, int64_t ldy, void* workspace,
                                     size_t workspace_bytes, void* stream) {
     return linear_impl(x, m, k, groups, trellis, n, K, codebook, suh, svh, y, ldy, workspace, workspace_bytes,
-                       stream);
+                       stream, nullptr);
+}
+
+extern "C" size_t exl3b_tp_comm_bytes(int tp_size, int max_blocks, int max_rows) {
+    if (tp_size < 2 || tp_size > EXL3B_MAX_TP || max_blocks < 1 || max_rows < 1 || max_rows > EXL3B_GEMV_MAX_ROWS)
+        return 0;
+    return tp_comm_bytes(tp_size, max_blocks, max_rows);
+}
+
+// Base of the allocation holding p, through the driver's cuMemGetAddressRange looked up at run
+// time (the library does not link the driver, so that it loads on machines without one).
+static bool allocation_base(const void* p, CUdeviceptr* base) {
+    using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(f);
+    });
+    size_t size = 0;
+    return fn && fn(base, &size, (CUdeviceptr)p) == CUDA_SUCCESS;
+}
+
+// The handle names the whole allocation; the offset of dev_ptr inside it travels alongside.
+extern "C" int exl3b_ipc_get_handle(const void* dev_ptr, void* handle) {
+    if (!dev_ptr || !handle) return EXL3B_BAD_ARG;
+    CUdeviceptr base = 0;
+    if (!allocation_base(dev_ptr, &base)) return EXL3B_BAD_ARG;
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return cuda_status(e);
+    const int64_t off = (int64_t)((CUdeviceptr)dev_ptr - base);
+    static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(int64_t) == EXL3B_IPC_HANDLE_BYTES, "handle layout");
+    memcpy(handle, &h, sizeof(h));
+    memcpy(static_cast<uint8_t*>(handle) + sizeof(h), &off, sizeof(off));
+    return EXL3B_OK;
+}
+
+extern "C" int exl3b_ipc_open_handle(const void* handle, void** dev_ptr) {
+    if (!handle || !dev_ptr) return EXL3B_BAD_ARG;
+    cudaIpcMemHandle_t h;
+    int64_t off = 0;
+    memcpy(&h, handle, sizeof(h));
+    memcpy(&off, static_cast<const uint8_t*>(handle) + sizeof(h), sizeof(off));
+    void* base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_status(e);
+    *dev_ptr = static_cast<uint8_t*>(base) + off;
+    return EXL3B_OK;
+}
+
+extern "C" int exl3b_ipc_close(void* dev_ptr) {
+    if (!dev_ptr) return EXL3B_BAD_ARG;
+    CUdeviceptr base = 0;
+    if (!allocation_base(dev_ptr, &base)) return EXL3B_BAD_ARG;
+    return cuda_status(cudaIpcCloseMemHandle(reinterpret_cast<void*>(base)));
+}
+
+extern "C" int exl3b_linear_tp(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K, int codebook,
+                               const uint16_t* suh, const uint16_t* svh, uint16_t* y, int64_t ldy, void* workspace,
+                               size_t workspace_bytes, const exl3b_tp_comm* comm, void* stream) {
+    if (!comm) return EXL3B_BAD_ARG;
+    const uint16_t* tr[1] = {trellis};
+    const uint16_t* su[1] = {suh};
+    const uint16_t* sv[1] = {svh};
+    uint16_t* yy[1] = {y};
+    int nn[1] = {n};
+    return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, workspace, workspace_bytes, stream, comm);
 }
 
 extern "C" int exl3b_linear_workspace_error(const void* workspace, int* out, void* stream) {

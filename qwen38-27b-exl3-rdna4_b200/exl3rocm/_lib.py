@@ -21,6 +21,16 @@ c_u16p = ctypes.c_void_p
 c_vp = ctypes.c_void_p
 i32, i64, f32, sz = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
+EXL3B_MAX_TP = 8
+EXL3B_IPC_HANDLE_BYTES = 72
+
+
+class TpComm(ctypes.Structure):
+    """exl3b_tp_comm of include/exl3b.h."""
+    _fields_ = [("tp_size", ctypes.c_int), ("tp_rank", ctypes.c_int), ("max_blocks", ctypes.c_int),
+                ("max_rows", ctypes.c_int), ("buffers", ctypes.c_void_p * EXL3B_MAX_TP)]
+
+
 # name -> (restype, argtypes); every symbol include/exl3b.h declares
 SIGNATURES = {
     "exl3b_version": (i32, []),
@@ -39,6 +49,12 @@ SIGNATURES = {
                                   i32, c_vp]),
     "exl3b_kv_int4_write": (i32, [c_vp, c_vp, i32, i64, i32, i32, i64, i64, i64, i64, c_vp, c_vp, c_vp, c_vp, c_vp,
                                   i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, i32, c_vp, c_vp, c_vp, c_vp]),
+    "exl3b_tp_comm_bytes": (sz, [i32, i32, i32]),
+    "exl3b_ipc_get_handle": (i32, [c_vp, c_vp]),
+    "exl3b_ipc_open_handle": (i32, [c_vp, ctypes.POINTER(c_vp)]),
+    "exl3b_ipc_close": (i32, [c_vp]),
+    "exl3b_linear_tp": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp, sz,
+                              ctypes.POINTER(TpComm), c_vp]),
     "exl3b_kv_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
     "exl3b_kv_int8_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,
                                  i32, i32, i32, f32, c_vp, sz, c_vp]),
