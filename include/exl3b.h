@@ -42,6 +42,9 @@ extern "C" {
 #define EXL3B_CB_3INST 0
 #define EXL3B_CB_MCG 1
 #define EXL3B_CB_MUL1 2
+/* or-ed into the codebook argument of the m <= 16 linears: x is bf16 and is rounded to fp16 inside
+ * the kernel, exactly as the reference's x.to(float16) at the op boundary (ops.py:72-73) */
+#define EXL3B_X_BF16 0x100
 
 #define EXL3B_MAX_GROUPS 8
 #define EXL3B_GEMV_MAX_ROWS 16

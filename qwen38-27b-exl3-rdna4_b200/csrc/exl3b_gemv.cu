@@ -56,7 +56,8 @@ struct GemvGroups {
 
 struct GemvParams {
     GemvGroups g;
-    const __half* x;      // [m][k]
+    const void* x;        // [m][k] fp16, or bf16 when x_bf16
+    int x_bf16;
     const __half* suh[EXL3B_MAX_GROUPS];
     float* partials;      // workspace: [ctas + super-blocks - 1][m][sb_cols], slot = cta + super-block
     int* counters;        // workspace: one per global column block
@@ -71,23 +72,24 @@ struct GemvParams {
     uint8_t* tp_buf[EXL3B_MAX_TP];
 };
 
-// Communication buffer of one rank: a 256-byte header (call counter, finished-CTA counter), flags
-// [2 parities][tp ranks][blocks] int32, then data [2][tp][blocks][rows][128] fp32.  Rank s writes
-// its partial of block b for call e into every rank's slot [e & 1][s][b] and then the flag, set to e.
+// Communication buffer of one rank: a 256-byte header (call counter, finished-CTA counter), then
+// slots [2 parities][tp ranks][blocks][rows][128] of (fp32 value, call number) pairs, 8 bytes each.
+// Rank s writes its partial of block b for call e into slot [e & 1][s][b] of every rank with 16-byte
+// volatile stores of two such pairs; a reader polls its own slot until every pair carries e, so data
+// and flag arrive together and no fence is needed (the low-latency protocol of NCCL's LL).
 constexpr size_t kTpHeader = 256;
-__host__ __device__ inline size_t tp_flag_bytes(int tp, int blocks) {
-    return ((size_t)2 * tp * blocks * 4 + 255) / 256 * 256;
-}
 __host__ __device__ inline size_t tp_comm_bytes(int tp, int blocks, int rows) {
-    return kTpHeader + tp_flag_bytes(tp, blocks) + (size_t)2 * tp * blocks * rows * 128 * 4;
+    return kTpHeader + (size_t)2 * tp * blocks * rows * 128 * 8;
 }
 
-EXL3B_DEV void st_release_sys(int* p, int v) {
-    asm volatile("st.release.sys.global.b32 [%0], %1;\n" :: "l"(p), "r"(v) : "memory");
+EXL3B_DEV void st_pairs(uint32_t* p, float a, float b, int ep) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};\n"
+                 :: "l"(p), "r"(__float_as_uint(a)), "r"(ep), "r"(__float_as_uint(b)), "r"(ep) : "memory");
 }
-EXL3B_DEV int ld_acquire_sys(const int* p) {
-    int v;
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+EXL3B_DEV uint4 ld_pairs(const uint32_t* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
     return v;
 }
 
@@ -213,55 +215,47 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
                 finish_row(row, v);
             }
         } else {
-            // Exchange this rank's k-slice partial of block b with every rank: data into
-            // slot [par][rank][b] of each rank's buffer, a system fence, then the flags;
-            // wait for every rank's flag of this call in our own buffer, sum in rank order.
+            // Exchange this rank's k-slice partial of block b with every rank: (value, call) pairs
+            // into slot [par][rank][b] of each rank's buffer; then poll our own slots of every rank
+            // until all pairs carry this call's number, and sum in rank order.
             const int tp = p.tp_size, rk = p.tp_rank, nb = p.tp_blocks, rows = p.tp_rows;
-            const int ep = ld_acquire_sys(reinterpret_cast<const int*>(p.tp_buf[rk])) + 1;
+            // the counter is written only by earlier kernels on this GPU (visible after griddepcontrol.wait)
+            const int ep = *reinterpret_cast<volatile const int*>(p.tp_buf[rk]) + 1;
             const int par = ep & 1;
-            const size_t fbytes = tp_flag_bytes(tp, nb);
+            auto slot = [&](int owner, int src, int row) {
+                return reinterpret_cast<uint32_t*>(p.tp_buf[owner] + kTpHeader) +
+                       ((((int64_t)par * tp + src) * nb + b) * rows + row) * 256 + 8 * lane;
+            };
             for (int row = 0; row < m; ++row) {
                 float v[4];
                 block_sum(row, v);
                 for (int r = 0; r < tp; ++r) {
-                    float* d = reinterpret_cast<float*>(p.tp_buf[r] + kTpHeader + fbytes) +
-                               ((((int64_t)par * tp + rk) * nb + b) * rows + row) * 128 + 4 * lane;
-                    __stcg(reinterpret_cast<float4*>(d), make_float4(v[0], v[1], v[2], v[3]));
+                    uint32_t* d = slot(r, rk, row);
+                    st_pairs(d, v[0], v[1], ep);
+                    st_pairs(d + 4, v[2], v[3], ep);
                 }
             }
-            __threadfence_system();
-            __syncwarp();
-            if (lane < tp)
-                st_release_sys(reinterpret_cast<int*>(p.tp_buf[lane] + kTpHeader) + ((int64_t)par * tp + rk) * nb + b, ep);
             bool ok = true;
-            if (lane < tp) {
-                const int* f = reinterpret_cast<const int*>(p.tp_buf[rk] + kTpHeader) + ((int64_t)par * tp + lane) * nb + b;
-                if (ld_acquire_sys(f) != ep) {
+            for (int row = 0; row < m; ++row) {
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int r = 0; r < tp; ++r) {  // fixed rank order: identical sums on every rank
+                    const uint32_t* q = slot(rk, r, row);
+                    uint4 a0 = ld_pairs(q), a1 = ld_pairs(q + 4);
                     const long long t0 = clock64();
-                    while (ld_acquire_sys(f) != ep) {
-                        if (clock64() - t0 > kWaitCycles) { ok = false; break; }
-                        __nanosleep(64);
+                    while (ok && (a0.y != (uint32_t)ep || a0.w != (uint32_t)ep || a1.y != (uint32_t)ep ||
+                                  a1.w != (uint32_t)ep)) {
+                        if (clock64() - t0 > kWaitCycles) ok = false;
+                        a0 = ld_pairs(q);
+                        a1 = ld_pairs(q + 4);
                     }
+                    v[0] += __uint_as_float(a0.x); v[1] += __uint_as_float(a0.z);
+                    v[2] += __uint_as_float(a1.x); v[3] += __uint_as_float(a1.z);
                 }
-            }
-            if (!__all_sync(0xFFFFFFFFu, ok)) {
-                if (lane == 0) { atomicExch(p.err, 6); *abort_flag = 1; }
-            } else {
-                // every lane acquires every flag itself, so that its own loads of the partials below
-                // are ordered after the peers' release stores
-                for (int r = 0; r < tp; ++r)
-                    (void)ld_acquire_sys(reinterpret_cast<const int*>(p.tp_buf[rk] + kTpHeader) +
-                                         ((int64_t)par * tp + r) * nb + b);
-                const float* mine = reinterpret_cast<const float*>(p.tp_buf[rk] + kTpHeader + fbytes);
-                for (int row = 0; row < m; ++row) {
-                    float v[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int r = 0; r < tp; ++r) {  // fixed rank order: identical sums on every rank
-                        const float4 t = __ldcg(reinterpret_cast<const float4*>(
-                            mine + ((((int64_t)par * tp + r) * nb + b) * rows + row) * 128 + 4 * lane));
-                        v[0] += t.x; v[1] += t.y; v[2] += t.z; v[3] += t.w;
-                    }
-                    finish_row(row, v);
+                if (!__all_sync(0xFFFFFFFFu, ok)) {
+                    if (lane == 0) { atomicExch(p.err, 6); *abort_flag = 1; }
+                    break;
                 }
+                finish_row(row, v);
             }
         }
         if (!whole && lane == 0) p.counters[Bg] = 0;
@@ -344,7 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             uint32_t* dst = reinterpret_cast<uint32_t*>(smem + (i % kStages) * S::kStageBytes + S::kTrellisStage +
                                                         (ktl - t0) * m * 32) + (slot >> 1);
             for (int row = 0; row < m; ++row) {
-                const uint2 xr = *reinterpret_cast<const uint2*>(p.x + (int64_t)row * p.k + col);
+                uint2 xr = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + (int64_t)row * p.k + col);
+                if (p.x_bf16) {  // bf16 -> fp16, round to nearest even (torch's .to(float16))
+                    const __nv_bfloat162 b01 = *reinterpret_cast<const __nv_bfloat162*>(&xr.x);
+                    const __nv_bfloat162 b23 = *reinterpret_cast<const __nv_bfloat162*>(&xr.y);
+                    xr.x = h2_as_u32(__floats2half2_rn(__low2float(b01), __high2float(b01)));
+                    xr.y = h2_as_u32(__floats2half2_rn(__low2float(b23), __high2float(b23)));
+                }
                 const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
                 const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
                 float v[4] = {__low2float(p01), __high2float(p01), __low2float(p23), __high2float(p23)};
@@ -612,6 +612,8 @@ static cudaError_t launch_gemv_k(int K, const GemvParams& p, cudaStream_t st) {
 int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis, const int* n,
                 int K, int codebook, const uint16_t* const* suh, const uint16_t* const* svh, uint16_t* const* y,
                 int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm) {
+    const bool x_bf16 = (codebook & EXL3B_X_BF16) != 0;
+    codebook &= ~EXL3B_X_BF16;
     if (K < 1 || K > 8 || codebook < 0 || codebook > 2) return EXL3B_DECLINED;
     if (m < 1 || m > EXL3B_GEMV_MAX_ROWS || groups < 1 || groups > EXL3B_MAX_GROUPS) return EXL3B_DECLINED;
     if (k <= 0 || k % 128) return EXL3B_DECLINED;
@@ -660,7 +662,8 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     }
     p.g.blk_prefix[groups] = blk;
     p.g.sb_prefix[groups] = sbs;
-    p.x = reinterpret_cast<const __half*>(x);
+    p.x = x;
+    p.x_bf16 = x_bf16 ? 1 : 0;
     p.partials = reinterpret_cast<float*>(ws + L.partials);
     p.counters = reinterpret_cast<int*>(ws + L.counters);
     p.err = reinterpret_cast<int*>(ws);

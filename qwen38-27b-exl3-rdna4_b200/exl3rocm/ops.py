@@ -21,6 +21,7 @@ from . import _lib
 
 GEMV_MAX_ROWS = 16
 MAX_GROUPS = 8
+X_BF16 = 0x100  # EXL3B_X_BF16: x is bf16, rounded to fp16 inside the kernel
 RECON_SLICE_N = 17408  # widest model layer, as the reference (ops.py:22-24)
 
 _ws: dict = {}    # (device index, stream handle) -> uint8 workspace (counters zeroed once)
@@ -126,13 +127,14 @@ def had_r_128(inp: torch.Tensor, out: torch.Tensor, pre: Optional[torch.Tensor],
 
 def linear_into(x2: torch.Tensor, trellis: list, suh: list, svh: list, K: int, mcg: bool, mul1: bool,
                 y: torch.Tensor) -> None:
-    """Fused M <= 16 linear of groups sharing x and K; group i -> its column slice of y."""
+    """Fused M <= 16 linear of groups sharing x and K; group i -> its column slice of y.  x2 is fp16,
+    or bf16 (rounded to fp16 inside the kernel, as the reference's cast at the op boundary)."""
     M, k = x2.shape
     ng = len(trellis)
     widths = [int(s.shape[0]) for s in svh]
     ws = reserve_workspace(x2.device, k, sum(widths), ng, max(M, 1))
     st = _stream(x2.device)
-    cb = _cb(mcg, mul1)
+    cb = _cb(mcg, mul1) | (X_BF16 if x2.dtype == torch.bfloat16 else 0)
     if ng == 1:
         _lib.call("exl3b_linear", x2.data_ptr(), M, k, trellis[0].data_ptr(), widths[0], K, cb,
                   suh[0].data_ptr(), svh[0].data_ptr(), y.data_ptr(), y.stride(0), ws.data_ptr(), ws.numel(), st)
@@ -147,9 +149,10 @@ def linear_into(x2: torch.Tensor, trellis: list, suh: list, svh: list, K: int, m
               ys, y.stride(0), ws.data_ptr(), ws.numel(), st)
 
 
-def _prep_x(x: torch.Tensor, k: int) -> torch.Tensor:
+def _prep_x(x: torch.Tensor, k: int, keep_bf16: bool = False) -> torch.Tensor:
+    """[M, k] contiguous fp16 (or bf16 when keep_bf16: the m <= 16 kernels round it themselves)."""
     x2 = x.reshape(-1, k)
-    if x2.dtype != torch.float16:
+    if x2.dtype != torch.float16 and not (keep_bf16 and x2.dtype == torch.bfloat16):
         x2 = x2.to(torch.float16)
     if not x2.is_contiguous():
         x2 = x2.contiguous()
@@ -180,7 +183,7 @@ def exl3_linear(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: 
                 K: int, mcg: bool, mul1: bool) -> torch.Tensor:
     k = x.shape[-1]
     n = svh.shape[0]
-    x2 = _prep_x(x, k)
+    x2 = _prep_x(x, k, keep_bf16=(x.numel() // max(k, 1)) <= GEMV_MAX_ROWS)
     M = x2.shape[0]
     y = torch.empty((M, n), dtype=torch.float16, device=x.device)
     if M == 0:
@@ -208,7 +211,7 @@ def exl3_linear_groups(x: torch.Tensor, trellis: list[torch.Tensor], suh: list[t
     travel by value in the kernel parameters."""
     k = x.shape[-1]
     widths = [int(s.shape[0]) for s in svh]
-    x2 = _prep_x(x, k)
+    x2 = _prep_x(x, k, keep_bf16=(x.numel() // max(k, 1)) <= GEMV_MAX_ROWS)
     M = x2.shape[0]
     if len(trellis) == 1:
         return exl3_linear(x, trellis[0], suh[0], svh[0], K[0], mcg, mul1)

@@ -20,7 +20,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .ops import GEMV_MAX_ROWS, _cb, _prep_x, _stream, reserve_workspace
+from .ops import GEMV_MAX_ROWS, X_BF16, _cb, _prep_x, _stream, reserve_workspace
 
 
 class TpComm:
@@ -66,13 +66,14 @@ def linear_tp(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: to
     """Full output of a row-parallel EXL3 linear from this rank's input slice x [..., k/tp]."""
     k = x.shape[-1]
     n = svh.shape[0]
-    x2 = _prep_x(x, k)
+    x2 = _prep_x(x, k, keep_bf16=True)
     M = x2.shape[0]
     if not 1 <= M <= GEMV_MAX_ROWS:
         raise ValueError(f"exl3rocm: linear_tp takes 1..{GEMV_MAX_ROWS} rows, got {M}")
     y = torch.empty((M, n), dtype=torch.float16, device=x.device)
     ws = reserve_workspace(x.device, k, n, 1, max(M, 1))
-    _lib.call("exl3b_linear_tp", x2.data_ptr(), M, k, trellis.data_ptr(), n, K, _cb(mcg, mul1), suh.data_ptr(),
+    cb = _cb(mcg, mul1) | (X_BF16 if x2.dtype == torch.bfloat16 else 0)
+    _lib.call("exl3b_linear_tp", x2.data_ptr(), M, k, trellis.data_ptr(), n, K, cb, suh.data_ptr(),
               svh.data_ptr(), y.data_ptr(), y.stride(0), ws.data_ptr(), ws.numel(), ctypes.byref(comm.comm),
               _stream(x.device))
     return y.view(*x.shape[:-1], n)

@@ -293,3 +293,18 @@ def test_linear_large_m_route(ops, m):
     y = torch.ops.exl3rocm.linear(xd, td, sd, vd, 4, False, True)
     st = stats(y.cpu().numpy(), O.linear(x, tr, 4, suh, svh, 2))
     assert st["normalized_rms_err"] < 2e-3 and st["cosine_similarity"] > 0.99999, st
+
+
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_bf16_input_rounded_in_kernel_matches_cast(ops, m):
+    """bf16 x is rounded to fp16 inside the kernel: bitwise the same as the reference's cast at the op
+    boundary (vllm_plugin/exl3rocm/ops.py:72-73), for one group and for a grouped call."""
+    x, tr, suh, svh = fixtures(1024, 512, 4, 31 + m, m=m)
+    xb = torch.randn(m, 1024, device=DEV, dtype=torch.float32).to(torch.bfloat16)
+    _, td, sd, vd = to_dev(x, tr, suh, svh)
+    y_bf = torch.ops.exl3rocm.linear(xb, td, sd, vd, 4, False, True)
+    y_fp = torch.ops.exl3rocm.linear(xb.to(torch.float16), td, sd, vd, 4, False, True)
+    assert torch.equal(y_bf, y_fp)
+    g_bf = torch.ops.exl3rocm.linear_groups(xb, [td, td], [sd, sd], [vd, vd], [4, 4], False, True)
+    g_fp = torch.ops.exl3rocm.linear_groups(xb.to(torch.float16), [td, td], [sd, sd], [vd, vd], [4, 4], False, True)
+    assert torch.equal(g_bf, g_fp)
