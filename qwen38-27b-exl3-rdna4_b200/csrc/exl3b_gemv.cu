@@ -63,7 +63,8 @@ struct GemvParams {
     int* counters;        // workspace: one per global column block
     int* err;             // workspace error word
     int groups, m, k, kt;  // kt = k / 16
-    int ku;               // units per super-block = kt / R
+    int ku;               // units per super-block = kt / (R0 * q)
+    int q;                // k-rows per 64-tile stage slot (super-blocks of 64 / q n-tiles): 1, 2 or 4
     int units, ctas;
     int sb_cols;          // widest super-block of the call, in columns
     int64_t ldy;
@@ -121,11 +122,11 @@ EXL3B_DEV SbInfo sb_info(const GemvGroups& gg, int groups, int sb) {
 // warps pool a finished super-block, and the mbarriers.
 template <int K, int MT>
 struct GemvSmem {
-    static constexpr int R = rows_per_unit(K);
+    static constexpr int R0 = rows_per_unit(K);           // stage slots of 64 tiles
     static constexpr int kTile = 32 * K;                  // bytes of one 16x16 tile
-    static constexpr int kRowBytes = kSbTiles * kTile;    // stride of the unit's rows in a stage
-    static constexpr int kTrellisStage = R * kRowBytes;
-    static constexpr int kAhadStage = R * 8 * MT * 32;    // R k-tiles x 8 MT rows x 16 halves
+    static constexpr int kRowBytes = kSbTiles * kTile;    // stride of the stage slots
+    static constexpr int kTrellisStage = R0 * kRowBytes;
+    static constexpr int kAhadStage = 4 * R0 * 8 * MT * 32;  // up to 4 R0 k-tiles x 8 MT rows x 16 halves
     static constexpr int kStageBytes = kTrellisStage + kAhadStage;
     static constexpr int kAccBytes = 8 * MT * kAccCols * 4;
     static constexpr int kBudget = 220 * 1024;
@@ -266,7 +267,8 @@ template <int K, int CB, int MT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     using S = GemvSmem<K, MT>;
     constexpr int kStages = S::kStages;
-    constexpr int R = S::R;
+    constexpr int R0 = S::R0;
+    const int q = p.q, R = R0 * p.q;  // k-rows per unit; row r sits in slot r / q at tile (r % q) * 64 / q
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t sbase = smem_u32(smem);
@@ -317,41 +319,45 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             if (lane < R) {
                 const uint16_t* src =
                     p.g.trellis[si.g] + ((int64_t)(kr0 + lane) * p.g.n_tiles[si.g] + si.b0 * 8) * (16 * K);
-                bulk_g2s(sbase + s * S::kStageBytes + lane * S::kRowBytes, src, row_bytes, full0 + 8 * s);
+                const uint32_t dst = sbase + s * S::kStageBytes + (lane / q) * S::kRowBytes +
+                                     (lane % q) * (kSbTiles / q) * S::kTile;
+                bulk_g2s(dst, src, row_bytes, full0 + 8 * s);
             }
             issued = i + 1;
             return true;
         };
-        // A_had of the unit's R k-tiles (inside one 128-input block) for rows 0..m-1, as
-        // fp16(H128 fp16(x * suh) / sqrt(128)); lane l transforms inputs 4l..4l+3 of the block,
-        // which sit in k-tile l/4 at fragment slots kk = 2q + b -> 4q + b, 8 + 2q + b -> 4q + 2 + b
+        // A_had of the unit's R k-tiles for rows 0..m-1, as fp16(H128 fp16(x * suh) / sqrt(128)), one
+        // 128-input block at a time; lane l transforms inputs 4l..4l+3 of a block, which sit in
+        // k-tile l/4 at fragment slots kk = 2q + b -> 4q + b, 8 + 2q + b -> 4q + 2 + b
         const int ktl = lane >> 2, kq = lane & 3;
-        const int slot = (kq < 2) ? 8 * kq : 8 * (kq - 2) + 2;
+        const int fslot = (kq < 2) ? 8 * kq : 8 * (kq - 2) + 2;
         auto transform = [&](int i) {
             const int u = u0 + i;
             locate(u);
             const int kr0 = (u - sb * ku) * R;
-            const int blk = kr0 >> 3, t0 = kr0 & 7;
-            const int col = blk * 128 + 4 * lane;
-            const uint2 sr = *reinterpret_cast<const uint2*>(p.suh[si.g] + col);
-            const bool mine = ktl >= t0 && ktl < t0 + R;
-            uint32_t* dst = reinterpret_cast<uint32_t*>(smem + (i % kStages) * S::kStageBytes + S::kTrellisStage +
-                                                        (ktl - t0) * m * 32) + (slot >> 1);
-            for (int row = 0; row < m; ++row) {
-                uint2 xr = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + (int64_t)row * p.k + col);
-                if (p.x_bf16) {  // bf16 -> fp16, round to nearest even (torch's .to(float16))
-                    const __nv_bfloat162 b01 = *reinterpret_cast<const __nv_bfloat162*>(&xr.x);
-                    const __nv_bfloat162 b23 = *reinterpret_cast<const __nv_bfloat162*>(&xr.y);
-                    xr.x = h2_as_u32(__floats2half2_rn(__low2float(b01), __high2float(b01)));
-                    xr.y = h2_as_u32(__floats2half2_rn(__low2float(b23), __high2float(b23)));
-                }
-                const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
-                const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
-                float v[4] = {__low2float(p01), __high2float(p01), __low2float(p23), __high2float(p23)};
-                had128_warp(v);
-                if (mine) {
-                    dst[row * 8] = h2_as_u32(__floats2half2_rn(v[0] * kRScale, v[1] * kRScale));
-                    dst[row * 8 + 2] = h2_as_u32(__floats2half2_rn(v[2] * kRScale, v[3] * kRScale));
+            for (int blk = kr0 >> 3; blk <= (kr0 + R - 1) >> 3; ++blk) {
+                const int col = blk * 128 + 4 * lane;
+                const int kt = blk * 8 + ktl;  // this lane's k-tile
+                const bool mine = kt >= kr0 && kt < kr0 + R;
+                const uint2 sr = *reinterpret_cast<const uint2*>(p.suh[si.g] + col);
+                uint32_t* dst = reinterpret_cast<uint32_t*>(smem + (i % kStages) * S::kStageBytes + S::kTrellisStage +
+                                                            (kt - kr0) * m * 32) + (fslot >> 1);
+                for (int row = 0; row < m; ++row) {
+                    uint2 xr = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + (int64_t)row * p.k + col);
+                    if (p.x_bf16) {  // bf16 -> fp16, round to nearest even (torch's .to(float16))
+                        const __nv_bfloat162 b01 = *reinterpret_cast<const __nv_bfloat162*>(&xr.x);
+                        const __nv_bfloat162 b23 = *reinterpret_cast<const __nv_bfloat162*>(&xr.y);
+                        xr.x = h2_as_u32(__floats2half2_rn(__low2float(b01), __high2float(b01)));
+                        xr.y = h2_as_u32(__floats2half2_rn(__low2float(b23), __high2float(b23)));
+                    }
+                    const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
+                    const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
+                    float v[4] = {__low2float(p01), __high2float(p01), __low2float(p23), __high2float(p23)};
+                    had128_warp(v);
+                    if (mine) {
+                        dst[row * 8] = h2_as_u32(__floats2half2_rn(v[0] * kRScale, v[1] * kRScale));
+                        dst[row * 8 + 2] = h2_as_u32(__floats2half2_rn(v[2] * kRScale, v[3] * kRScale));
+                    }
                 }
             }
         };
@@ -401,30 +407,55 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
+    // Stage position w + 16 j of a slot holds k-row (slot * q + j / wq) and n-tile (w + 16 (j % wq)) of
+    // the super-block, wq = 4 / q: with q = 1 a warp covers four n-tiles of one k-row, with q = 4 one
+    // n-tile of four k-rows (acc[j] then hold partial sums of the same columns, folded at the flush).
+    const int wq = 4 / q;
+    uint32_t jb[4];  // A_had offset of position j's k-row inside its slot
+#pragma unroll
+    for (int j = 0; j < 4; ++j) jb[j] = (uint32_t)(j / wq) * mstride;
     int sb = u0 / ku;
     SbInfo si = sb_info(p.g, p.groups, sb);
-    int nj = 0;  // n-tiles of this warp in the current super-block
-    while (nj < 4 && warp + 16 * nj < si.nblk * 8) ++nj;
+    auto valid_mask = [&](int nt) {
+        int v = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (warp + 16 * (j % wq) < nt) v |= 1 << j;
+        return v;
+    };
+    int vmask = valid_mask(si.nblk * 8);  // positions of this warp that hold a tile in this super-block
 
-    // one unit: R k-tile rows x this warp's n-tiles (all four when FULL, else the first nj)
-    auto unit = [&](const uint8_t* st, auto full_tag) {
+    // one unit: R0 slots x this warp's four positions (all of them when FULL, else those in vmask)
+    auto unit = [&](const uint8_t* st, auto full_tag, auto q1_tag) {
         constexpr bool FULL = decltype(full_tag)::value;
+        constexpr bool Q1 = decltype(q1_tag)::value;  // q == 1: one k-row per slot, one B fragment
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
+        for (int r = 0; r < R0; ++r) {
+            const uint8_t* bs = st + boff + (uint32_t)(r * q) * mstride;
             uint32_t b[MT][2];
+            if (Q1) {
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                const uint2 v = *reinterpret_cast<const uint2*>(st + boff + r * mstride + mt * 8 * 32);
-                b[mt][0] = v.x;
-                b[mt][1] = v.y;
+                for (int mt = 0; mt < MT; ++mt) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(bs + mt * 8 * 32);
+                    b[mt][0] = v.x;
+                    b[mt][1] = v.y;
+                }
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                if (FULL || j < nj) {
+                if (FULL || ((vmask >> j) & 1)) {
+                    if (!Q1) {
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            const uint2 v = *reinterpret_cast<const uint2*>(bs + jb[j] + mt * 8 * 32);
+                            b[mt][0] = v.x;
+                            b[mt][1] = v.y;
+                        }
+                    }
                     uint32_t Wd[LaneGeom<K>::kNW];
 #pragma unroll
-                    for (int q = 0; q < LaneGeom<K>::kNW; ++q)
-                        Wd[q] = *reinterpret_cast<const uint32_t*>(st + woff[q] + r * S::kRowBytes + j * 16 * S::kTile);
+                    for (int qq = 0; qq < LaneGeom<K>::kNW; ++qq)
+                        Wd[qq] = *reinterpret_cast<const uint32_t*>(st + woff[qq] + r * S::kRowBytes + j * 16 * S::kTile);
                     uint32_t a[4];
                     lane_decode_frag<K, CB>(Wd, geom.phi, a);
 #pragma unroll
@@ -442,8 +473,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         if (__all_sync(0xFFFFFFFFu, ok)) {
             const uint8_t* st = smem + s * S::kStageBytes;
             // the unguarded copy only where registers allow it (one m-tile)
-            if (MT == 1 && nj == 4) unit(st, std::true_type{});
-            else if (nj > 0) unit(st, std::false_type{});
+            if (MT == 1 && vmask == 0xF) {
+                if (q == 1) unit(st, std::true_type{}, std::true_type{});
+                else unit(st, std::true_type{}, std::false_type{});
+            } else if (vmask) {
+                if (q == 1) unit(st, std::false_type{}, std::true_type{});
+                else unit(st, std::false_type{}, std::false_type{});
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * s);
@@ -455,13 +491,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         // ---------------- pool the finished super-block, then one warp per column block ----------------
         griddep_wait();  // the workspace counters and y may still belong to the previous kernel
         named_bar(kFlushBar, kDecodeWarps * 32);  // the previous flush's readers are done with acc_s
+        // positions j and j + wq hold the same columns when q > 1: fold them, in a fixed order
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (q >= 2) {
+                    acc[mt][0][e] += acc[mt][2][e];
+                    acc[mt][1][e] += acc[mt][3][e];
+                }
+                if (q == 4) acc[mt][0][e] += acc[mt][1][e];
+            }
         // fragment -> acc_s[row][col]: lane (gq, tq) holds D[col gq (+8)][rows 2tq, 2tq+1] of n-tile
-        // warp + 16 j
+        // warp + 16 j, j < wq
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                if (j < nj) {
+                if (j < wq && ((vmask >> j) & 1)) {
                     const int col = (warp + 16 * j) * 16 + gq;
                     const int r0 = 8 * mt + 2 * tq;
                     if (r0 < m) {
@@ -482,8 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         if (i + 1 < nunits) {
             ++sb;
             si = sb_info(p.g, p.groups, sb);
-            nj = 0;
-            while (nj < 4 && warp + 16 * nj < si.nblk * 8) ++nj;
+            vmask = valid_mask(si.nblk * 8);
         }
     }
     if (p.tp_size > 1) {
@@ -531,30 +577,41 @@ static int num_sms() {
 static int gemv_ctas(int units) { return std::min(units, num_sms()); }
 
 // Super-blocks of one group: its 128-column blocks split as evenly as possible into runs of at
-// most 8 (1024 columns).
-static void split_super_blocks(int blocks, int& count, int& base, int& extra) {
-    count = (blocks + 7) / 8;
+// most `maxb` (8 / q: 1024, 512 or 256 columns).
+static void split_super_blocks(int blocks, int maxb, int& count, int& base, int& extra) {
+    count = (blocks + maxb - 1) / maxb;
     base = blocks / count;
     extra = blocks % count;
 }
 
 struct Partition {
-    int ku, units, ctas, sb_cols, super_blocks;
+    int q, ku, units, ctas, sb_cols, super_blocks;
 };
 
+// The widest super-blocks (smallest q) that still give every column block at most about eight
+// CTAs to reduce over: narrow layers (o, down, k/v) get 256- or 512-column super-blocks with more
+// k-rows per unit, so that their cross-CTA sums stay short.  Depends on the shape and K only.
 static Partition partition(int k, int K, int groups, const int* n) {
+    const int kt = k / 16, r0 = rows_per_unit(K);
     Partition q = {};
-    q.ku = (k / 16) / rows_per_unit(K);
-    int widest = 0;
-    for (int g = 0; g < groups; ++g) {
-        int cnt, base, extra;
-        split_super_blocks(n[g] / 128, cnt, base, extra);
-        q.super_blocks += cnt;
-        widest = std::max(widest, base + (extra ? 1 : 0));
+    for (int qq : {1, 2, 4}) {
+        if (kt % (r0 * qq)) break;  // rows per unit must divide k / 16
+        Partition t = {};
+        t.q = qq;
+        t.ku = kt / (r0 * qq);
+        int widest = 0;
+        for (int g = 0; g < groups; ++g) {
+            int cnt, base, extra;
+            split_super_blocks(n[g] / 128, 8 / qq, cnt, base, extra);
+            t.super_blocks += cnt;
+            widest = std::max(widest, base + (extra ? 1 : 0));
+        }
+        t.sb_cols = widest * 128;
+        t.units = t.super_blocks * t.ku;
+        t.ctas = gemv_ctas(std::max(t.units, 1));
+        q = t;
+        if (t.super_blocks * 8 >= num_sms()) break;
     }
-    q.sb_cols = widest * 128;
-    q.units = q.super_blocks * q.ku;
-    q.ctas = gemv_ctas(std::max(q.units, 1));
     return q;
 }
 
@@ -654,7 +711,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
         p.g.blk_prefix[g] = blk;
         p.g.sb_prefix[g] = sbs;
         int cnt, base, extra;
-        split_super_blocks(n[g] / 128, cnt, base, extra);
+        split_super_blocks(n[g] / 128, 8 / q.q, cnt, base, extra);
         p.g.sb_base[g] = base;
         p.g.sb_extra[g] = extra;
         blk += n[g] / 128;
@@ -672,6 +729,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     p.k = k;
     p.kt = k / 16;
     p.ku = q.ku;
+    p.q = q.q;
     p.units = q.units;
     p.ctas = q.ctas;
     p.sb_cols = q.sb_cols;
@@ -703,7 +761,7 @@ extern "C" size_t exl3b_linear_workspace_bytes(int m, int k, int groups, int64_t
     // an upper bound over every K and every split of n_total into `groups` widths
     const int64_t blocks = n_total / 128;
     Partition q = {};
-    q.super_blocks = (int)std::min<int64_t>(blocks, (blocks + 7) / 8 + groups - 1);
+    q.super_blocks = (int)std::min<int64_t>(blocks, (blocks + 1) / 2 + groups - 1);  // q = 4: 2 blocks each
     q.sb_cols = (int)std::min<int64_t>(blocks, 8) * 128;
     q.ctas = (int)std::min<int64_t>(num_sms(), (int64_t)q.super_blocks * ((k / 16) / rows_per_unit(8)));
     return ws_layout(m, k, groups, q).total;
