@@ -170,6 +170,21 @@ EXL3B_API int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_token
                                  const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
                                  const int32_t* seq_slots, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Prefill over the quantised caches: gather the blocks listed in block_ids (n entries) and dequantise
+ * them to fp16 rows out[n][block_size][num_kv_heads][128], for an fp16 attention kernel to read.
+ * int8: out = fp16(q * scale).  Replaces gather_dequant (reference vllm_plugin/exl3rocm/kv_dequant.py:42-152). */
+EXL3B_API int exl3b_kv_int8_gather(const int8_t* cache, const float* scale, int block_size, int num_kv_heads,
+                                   int head_size, const int32_t* block_ids, int64_t n, uint16_t* out, void* stream);
+/* int4: out = fp16((nibble - zp) * scale / sqrt(128)), still rotated but in the orthonormal domain;
+ * block_ids lists blocks_per_seq blocks per sequence, and with exact_tag given, positions whose exact row
+ * (first 4 / newest 128 of the sequence's request slot) carries a matching tag take that row / sqrt(128).
+ * Replaces gather_dequant_int4 + _tail_overlay (reference vllm_plugin/exl3rocm/kv_dequant.py:80-123,
+ * kv_int4.py:566-594). */
+EXL3B_API int exl3b_kv_int4_gather(const uint8_t* cache, const float* scale, int block_size, int num_kv_heads,
+                                   int head_size, const int32_t* block_ids, int64_t n, int blocks_per_seq,
+                                   uint16_t* out, const uint16_t* exact, const int32_t* exact_tag,
+                                   const int32_t* seq_slots, const int32_t* seq_lens, void* stream);
+
 /* exl3b_linear without a caller-provided workspace, for callers that cannot allocate device
  * memory: code that runs while a CUDA graph is being captured (cudaMalloc is not allowed there),
  * hosts whose device memory is owned by a pool the caller cannot reach, and latency-critical

@@ -800,6 +800,68 @@ __global__ void kv_reduce_kernel(const KvReduceArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// prefill: gather + dequantise the blocks a batch uses into an fp16 buffer (reference
+// vllm_plugin/exl3rocm/kv_dequant.py:42-152, kv_int4.py:566-621)
+// ---------------------------------------------------------------------------------------------
+struct KvGatherArgs {
+    const uint8_t* cache;        // [blocks][bs][H][row bytes]
+    const float* scale;          // [blocks][bs][H]
+    const int32_t* block_ids;    // [n]: nb blocks per sequence, sequence s at s*nb .. s*nb+nb-1
+    int64_t n;
+    int bs, H, nb;
+    __half* out;                 // [n][bs][H][128]
+    float mul;                   // int4: 1/sqrt(128), the orthonormal rotated domain; int8: 1
+    // int4 exact rows (optional): position p of sequence s is exact when its tag matches
+    const __half* exact; const int32_t* exact_tag; const int32_t* seq_slots; const int32_t* seq_lens;
+};
+
+// One warp per output row (block entry j, slot, head); lane l writes elements 4l..4l+3.
+template <int KV>
+__global__ void kv_gather_kernel(const KvGatherArgs a) {
+    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= a.n * a.bs * a.H) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t j = item / ((int64_t)a.bs * a.H);
+    const int rem = (int)(item - j * a.bs * a.H);
+    const int slot = rem / a.H, h = rem % a.H;
+    const int64_t row = ((int64_t)a.block_ids[j] * a.bs + slot) * a.H + h;
+    float v[4];
+    bool done = false;
+    if (KV == 4 && a.exact_tag) {
+        const int sq = (int)(j / a.nb);
+        const int pos = (int)(j % a.nb) * a.bs + slot;
+        const int L = a.seq_lens[sq], rs = a.seq_slots[sq];
+        if (rs >= 0 && pos < L && (pos < kSinks || pos >= L - kTail)) {
+            const int e = exact_row(pos);
+            if (a.exact_tag[(int64_t)rs * kExactRows + e] == pos) {
+                const uint2 w = *reinterpret_cast<const uint2*>(a.exact + (((int64_t)rs * kExactRows + e) * a.H + h) * kHD + 4 * lane);
+                const __half2 e01 = u32_as_h2(w.x), e23 = u32_as_h2(w.y);
+                v[0] = __low2float(e01) * a.mul; v[1] = __high2float(e01) * a.mul;
+                v[2] = __low2float(e23) * a.mul; v[3] = __high2float(e23) * a.mul;
+                done = true;
+            }
+        }
+    }
+    if (!done) {
+        if constexpr (KV == 8) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(a.cache + row * kHD + 4 * lane);
+            const float sc = a.scale[row];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = (float)(int8_t)((w >> (8 * i)) & 0xFFu) * sc;
+        } else {
+            const uint16_t w = *reinterpret_cast<const uint16_t*>(a.cache + row * (kHD / 2) + 2 * lane);
+            const uint32_t bits = __float_as_uint(a.scale[row]);
+            const float zp = (float)(bits & 0xFu);
+            const float sc = __uint_as_float(bits & 0xFFFFFFF0u) * a.mul;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = ((float)((w >> (4 * i)) & 0xFu) - zp) * sc;
+        }
+    }
+    *reinterpret_cast<uint2*>(a.out + item * kHD + 4 * lane) =
+        make_uint2(h2_as_u32(__floats2half2_rn(v[0], v[1])), h2_as_u32(__floats2half2_rn(v[2], v[3])));
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 static int kv_num_sms() {
@@ -990,4 +1052,40 @@ extern "C" int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_toke
                           k_scale, v_scale, block_size, block_table, bt_stride, seq_lens, query_start_loc, num_seqs,
                           max_q_len, max_seq_len, softmax_scale, rht_signs, exact_k, exact_v, exact_tag, seq_slots,
                           workspace, workspace_bytes, stream);
+}
+
+static int kv_gather_common(int kv, const void* cache, const float* scale, int block_size, int num_kv_heads,
+                            int head_size, const int32_t* block_ids, int64_t n, int blocks_per_seq, uint16_t* out,
+                            const uint16_t* exact, const int32_t* exact_tag, const int32_t* seq_slots,
+                            const int32_t* seq_lens, void* stream) {
+    if (head_size != kHD || block_size <= 0 || num_kv_heads <= 0 || blocks_per_seq <= 0) return EXL3B_DECLINED;
+    if (n < 0) return EXL3B_BAD_ARG;
+    if (n == 0) return EXL3B_OK;
+    if (!cache || !scale || !block_ids || !out) return EXL3B_BAD_ARG;
+    if (exact_tag && (!exact || !seq_slots || !seq_lens)) return EXL3B_BAD_ARG;
+    KvGatherArgs a = {};
+    a.cache = static_cast<const uint8_t*>(cache); a.scale = scale; a.block_ids = block_ids; a.n = n;
+    a.bs = block_size; a.H = num_kv_heads; a.nb = blocks_per_seq; a.out = reinterpret_cast<__half*>(out);
+    a.mul = kv == 4 ? 0.08838834764831845f : 1.f;
+    a.exact = reinterpret_cast<const __half*>(exact); a.exact_tag = exact_tag; a.seq_slots = seq_slots;
+    a.seq_lens = seq_lens;
+    const int64_t items = n * block_size * num_kv_heads;
+    const unsigned grid = (unsigned)((items + 7) / 8);
+    if (kv == 8) kv_gather_kernel<8><<<grid, 256, 0, (cudaStream_t)stream>>>(a);
+    else kv_gather_kernel<4><<<grid, 256, 0, (cudaStream_t)stream>>>(a);
+    return cuda_status(cudaGetLastError());
+}
+
+extern "C" int exl3b_kv_int8_gather(const int8_t* cache, const float* scale, int block_size, int num_kv_heads,
+                                    int head_size, const int32_t* block_ids, int64_t n, uint16_t* out, void* stream) {
+    return kv_gather_common(8, cache, scale, block_size, num_kv_heads, head_size, block_ids, n, 1, out, nullptr,
+                            nullptr, nullptr, nullptr, stream);
+}
+
+extern "C" int exl3b_kv_int4_gather(const uint8_t* cache, const float* scale, int block_size, int num_kv_heads,
+                                    int head_size, const int32_t* block_ids, int64_t n, int blocks_per_seq,
+                                    uint16_t* out, const uint16_t* exact, const int32_t* exact_tag,
+                                    const int32_t* seq_slots, const int32_t* seq_lens, void* stream) {
+    return kv_gather_common(4, cache, scale, block_size, num_kv_heads, head_size, block_ids, n, blocks_per_seq, out,
+                            exact, exact_tag, seq_slots, seq_lens, stream);
 }

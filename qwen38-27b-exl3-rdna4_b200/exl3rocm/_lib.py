@@ -56,6 +56,8 @@ SIGNATURES = {
     "exl3b_linear_tp": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp, sz,
                               ctypes.POINTER(TpComm), c_vp]),
     "exl3b_kv_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+    "exl3b_kv_int8_gather": (i32, [c_vp, c_vp, i32, i32, i32, c_vp, i64, c_vp, c_vp]),
+    "exl3b_kv_int4_gather": (i32, [c_vp, c_vp, i32, i32, i32, c_vp, i64, i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "exl3b_kv_int8_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,
                                  i32, i32, i32, f32, c_vp, sz, c_vp]),
     "exl3b_kv_int4_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,

@@ -223,3 +223,112 @@ def attention_int8(*, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block
     """int8 per-token-head paged decode / verify attention (vLLM unified attention, 3D split)."""
     _attn(8, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale, k_scale_cache,
           v_scale_cache, max_seqlen_k, None)
+
+
+# ---------------------------------------------------------------------------------------------
+# prefill over the quantised caches (reference kv_dequant.py:42-152, kv_int4.py:566-621,
+# plugin.py:586-636): gather + dequantise the blocks the batch uses into an fp16 buffer, then an
+# fp16 paged attention kernel over it (vLLM's, handed in as `orig`, or torch SDPA without one)
+# ---------------------------------------------------------------------------------------------
+_gather_bufs: dict = {}
+
+
+def _gather_buffer(tag, device, n, bs, heads) -> torch.Tensor:
+    """Persistent fp16 buffer [>= n][bs][heads][128] (grows, never shrinks: repeated prefill chunks
+    with growing context reuse it instead of ratcheting the caching allocator)."""
+    key = (tag, str(device), bs, heads)
+    buf = _gather_bufs.get(key)
+    if buf is None or buf.shape[0] < n:
+        grow = max(n, int((buf.shape[0] if buf is not None else 0) * 1.25) + 1)
+        buf = torch.empty((grow, bs, heads, HEAD_SIZE), dtype=torch.float16, device=device)
+        _gather_bufs[key] = buf
+    return buf[:n]
+
+
+def gather_dequant_int8(cache, scale, blocks, tag="k"):
+    """int8 cache rows of `blocks` -> fp16 [n, bs, heads, 128] = q * scale (kv_dequant.py:131-152)."""
+    bs, heads = cache.shape[1], cache.shape[2]
+    ids = blocks.to(torch.int32).contiguous()
+    out = _gather_buffer(tag, cache.device, ids.numel(), bs, heads)
+    _lib.call("exl3b_kv_int8_gather", cache.data_ptr(), scale.data_ptr(), bs, heads, HEAD_SIZE, ids.data_ptr(),
+              ids.numel(), out.data_ptr(), _stream(cache.device))
+    return out
+
+
+def gather_dequant_int4(cache, scale, blocks, nb, tag="k", exact=None, seq_lens=None):
+    """int4 cache rows -> fp16 [n, bs, heads, 128] in the orthonormal rotated domain; with `exact`
+    (the layer's exact rows for this side: (rows, tags)) the sequences' exact positions replace the
+    quantised ones (kv_dequant.py:80-123 + kv_int4.py:566-594)."""
+    bs, heads = cache.shape[1], cache.shape[2]
+    ids = blocks.to(torch.int32).contiguous()
+    out = _gather_buffer(tag, cache.device, ids.numel(), bs, heads)
+    use_ex = exact is not None and seq_lens is not None and _req["slot"] is not None
+    sl = seq_lens.to(torch.int32).contiguous() if use_ex else None
+    _lib.call("exl3b_kv_int4_gather", cache.data_ptr(), scale.data_ptr(), bs, heads, HEAD_SIZE, ids.data_ptr(),
+              ids.numel(), nb, out.data_ptr(), exact[0].data_ptr() if use_ex else None,
+              exact[1].data_ptr() if use_ex else None, _req["slot"].data_ptr() if use_ex else None,
+              sl.data_ptr() if use_ex else None, _stream(cache.device))
+    return out
+
+
+def _sdpa_paged(q, kd, vd, cu_seqlens_q, seqused_k, nb, softmax_scale, out):
+    """Causal GQA attention of each sequence's queries (the last q_len positions) over its nb gathered
+    blocks, with torch's scaled_dot_product_attention (fp16 in, fp32 softmax)."""
+    qsl = cu_seqlens_q.tolist()
+    lens = seqused_k.tolist()
+    bs = kd.shape[1]
+    for s, L in enumerate(lens):
+        q0, q1 = qsl[s], qsl[s + 1]
+        if q1 <= q0:
+            continue
+        ql = q1 - q0
+        k = kd[s * nb:(s + 1) * nb].reshape(nb * bs, kd.shape[2], HEAD_SIZE)[:L]
+        v = vd[s * nb:(s + 1) * nb].reshape(nb * bs, vd.shape[2], HEAD_SIZE)[:L]
+        # query i sits at position L - ql + i and sees keys 0 .. L - ql + i
+        mask = torch.arange(L, device=q.device)[None, :] <= (L - ql + torch.arange(ql, device=q.device))[:, None]
+        o = torch.nn.functional.scaled_dot_product_attention(
+            q[q0:q1].transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), attn_mask=mask, scale=softmax_scale,
+            enable_gqa=True)
+        out[q0:q1] = o.transpose(0, 1).to(out.dtype)
+
+
+def prefill(orig=None, kw=None, layer_name=None):
+    """int4 long prefill chunk (kv_int4.py:596-621): dequantise the sequences' blocks to fp16 in the
+    orthonormal rotated domain (exact rows overlaid), attend with an orthonormally rotated q, then
+    un-rotate the output.  q.k and p.v are unchanged by the rotation."""
+    q, k, v, bt, out = kw["q"], kw["k"], kw["v"], kw["block_table"], kw["out"]
+    bs = k.shape[1]
+    nb = (int(kw["max_seqlen_k"]) + bs - 1) // bs
+    flat = bt[:, :nb].reshape(-1)
+    ex = _exact.get(layer_name) if layer_name else None
+    kd = gather_dequant_int4(k, kw["k_scale_cache"], flat, nb, "k", (ex["k"], ex["tag"]) if ex else None,
+                             kw["seqused_k"])
+    vd = gather_dequant_int4(v, kw["v_scale_cache"], flat, nb, "v", (ex["v"], ex["tag"]) if ex else None,
+                             kw["seqused_k"])
+    s16 = rht_signs(q.device).to(torch.float16)
+    qr = torch.empty_like(q)
+    _lib.call("exl3b_had128", q.data_ptr(), HEAD_SIZE, qr.data_ptr(), HEAD_SIZE, q.numel() // HEAD_SIZE, HEAD_SIZE,
+              s16.data_ptr(), None, 1.0, _stream(q.device))  # H (q * s) / sqrt(128)
+    rot = torch.empty_like(q)
+    if orig is not None:
+        new_bt = torch.arange(flat.numel(), device=bt.device, dtype=bt.dtype).view(bt.shape[0], nb)
+        orig(**dict(kw, q=qr, k=kd, v=vd, out=rot, block_table=new_bt, k_scale_cache=None, v_scale_cache=None))
+    else:
+        _sdpa_paged(qr, kd, vd, kw["cu_seqlens_q"], kw["seqused_k"], nb, kw["softmax_scale"], rot)
+    _lib.call("exl3b_had128", rot.data_ptr(), HEAD_SIZE, out.data_ptr(), HEAD_SIZE, q.numel() // HEAD_SIZE,
+              HEAD_SIZE, None, s16.data_ptr(), 1.0, _stream(q.device))  # s * H rot / sqrt(128)
+
+
+def prefill_int8(orig=None, kw=None):
+    """int8 long prefill chunk (plugin.py:586-636): dequantise the sequences' blocks to fp16, attend."""
+    q, k, v, bt, out = kw["q"], kw["k"], kw["v"], kw["block_table"], kw["out"]
+    bs = k.shape[1]
+    nb = (int(kw["max_seqlen_k"]) + bs - 1) // bs
+    flat = bt[:, :nb].reshape(-1)
+    kd = gather_dequant_int8(k, kw["k_scale_cache"], flat, "k")
+    vd = gather_dequant_int8(v, kw["v_scale_cache"], flat, "v")
+    if orig is not None:
+        new_bt = torch.arange(flat.numel(), device=bt.device, dtype=bt.dtype).view(bt.shape[0], nb)
+        orig(**dict(kw, k=kd, v=vd, block_table=new_bt, k_scale_cache=None, v_scale_cache=None))
+    else:
+        _sdpa_paged(q, kd, vd, kw["cu_seqlens_q"], kw["seqused_k"], nb, kw["softmax_scale"], out)

@@ -266,3 +266,58 @@ def test_int4_close_to_fp16_cache(kv):
                              lambda s_, n: k[:n].astype(np.float64), lambda s_, n: v[:n].astype(np.float64))
     nrms, cos = nrms_cos(out.cpu().numpy(), ref)
     assert cos > 0.98 and nrms < 0.2, (nrms, cos)
+
+
+# ---------------------------------------------------------------------------------------------
+# prefill over the quantised caches: gather + dequantise to fp16, fp16 attention (SDPA here)
+# ---------------------------------------------------------------------------------------------
+# The fp16 buffer and the fp16 attention kernel (P rounded to fp16 before P.V) add their own
+# roundings to the decode path's: the gate is wider than ATOL.
+PREFILL_ATOL = {"nrms": 4e-3, "cos": 0.9999}
+
+
+def _prefill_kw(q, kc, vc, ks, vs, bt, seq_lens, q_lens, qsl):
+    return dict(q=torch.from_numpy(q).to(DEV), k=kc, v=vc,
+                out=torch.empty((q.shape[0], HQ, D), dtype=torch.float16, device=DEV),
+                cu_seqlens_q=torch.from_numpy(qsl).to(DEV), max_seqlen_q=max(q_lens),
+                seqused_k=torch.tensor(seq_lens, dtype=torch.int32, device=DEV),
+                block_table=torch.from_numpy(bt).to(DEV), softmax_scale=D ** -0.5, k_scale_cache=ks,
+                v_scale_cache=vs, max_seqlen_k=max(seq_lens))
+
+
+def test_int8_gather_matches_oracle_dequant(kv):
+    rng = np.random.default_rng(44)
+    bt, kc, vc, ks, vs, qsl, q = _int8_setup(rng, [100, 37], [1, 1])
+    blocks = torch.from_numpy(bt.reshape(-1).copy()).to(DEV)
+    got = kv.gather_dequant_int8(torch.from_numpy(kc).to(DEV), torch.from_numpy(ks).to(DEV), blocks).cpu().numpy()
+    ref = (kc[bt.reshape(-1)].astype(np.float32) * ks[bt.reshape(-1)][..., None]).astype(np.float16)
+    np.testing.assert_array_equal(got.view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("seq_lens,q_lens", [([600], [64]), ([40, 300], [40, 17]), ([2000, 64], [33, 64])])
+def test_int8_prefill(kv, seq_lens, q_lens):
+    rng = np.random.default_rng(sum(seq_lens) + 5 * sum(q_lens))
+    bt, kc, vc, ks, vs, qsl, q = _int8_setup(rng, seq_lens, q_lens)
+    ref = KV.int8_attention(q, kc, vc, ks, vs, bt, seq_lens, qsl, D ** -0.5)
+    kw = _prefill_kw(q, torch.from_numpy(kc).to(DEV), torch.from_numpy(vc).to(DEV), torch.from_numpy(ks).to(DEV),
+                     torch.from_numpy(vs).to(DEV), bt, seq_lens, q_lens, qsl)
+    kv.prefill_int8(None, kw)
+    nrms, cos = nrms_cos(kw["out"].cpu().numpy(), ref)
+    assert nrms <= PREFILL_ATOL["nrms"] and cos >= PREFILL_ATOL["cos"], (nrms, cos)
+
+
+@pytest.mark.parametrize("seq_lens,q_lens", [([700, 150], [64, 30]), ([200], [200])])
+def test_int4_prefill_with_exact_rows(kv, seq_lens, q_lens):
+    rng = np.random.default_rng(sum(seq_lens) + 9)
+    slots = [2, 0][: len(seq_lens)]
+    bt, dev, ora = _int4_world(kv, rng, seq_lens, q_lens, slots)
+    kc, vc, ks, vs = dev
+    ko, vo, kso, vso, exk, exv, tag = ora
+    qsl = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    q = rng.standard_normal((int(qsl[-1]), HQ, D)).astype(np.float16)
+    ref = KV.int4_attention(q, ko, vo, kso, vso, exk, exv, tag, slots, bt, seq_lens, qsl, D ** -0.5,
+                            KV.rht_signs(D))
+    kw = _prefill_kw(q, kc, vc, ks, vs, bt, seq_lens, q_lens, qsl)
+    kv.prefill(None, kw, layer_name="L0")
+    nrms, cos = nrms_cos(kw["out"].cpu().numpy(), ref)
+    assert nrms <= PREFILL_ATOL["nrms"] and cos >= PREFILL_ATOL["cos"], (nrms, cos)
