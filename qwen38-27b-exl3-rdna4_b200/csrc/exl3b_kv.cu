@@ -400,26 +400,27 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
             __syncwarp();
         }
         const uint32_t tb = wsm_u + (ti % SM::kRing) * SM::kTile;
-#pragma unroll
-        for (int j = 0; j < C16; ++j) {  // 32 rows x C16 chunks, C16 per lane per side
-            const int cidx = lane + 32 * j;
-            const int r = cidx / C16, ch = cidx % C16;
-            const int t = t0 + r;
-            if (t < t_hi) {
-                const int64_t blk = bt_win[(t >> lg) - win_base];
-                const int64_t row = ((blk << lg) + (t & bs_mask)) * a.num_kv_heads + kvh;
-                const uint32_t soff = r * RB + ((ch ^ (r & (C16 - 1))) * 16);
-                cp_async16(tb + soff, reinterpret_cast<const uint8_t*>(a.key_cache) + row * RB + ch * 16);
-                cp_async16(tb + SM::kRows + soff, reinterpret_cast<const uint8_t*>(a.value_cache) + row * RB + ch * 16);
-            }
+        // Lane l looks up token t0 + l once (block table, row index) and copies its two scales; the
+        // 16-byte chunks then go out coalesced (eight lanes per row) with each row index taken from
+        // the lane that looked it up.
+        const int t = t0 + lane;
+        uint32_t my_slot = 0xFFFFFFFFu;  // block * block_size + slot of token t: fits 32 bits for any cache
+        if (t < t_hi) {
+            my_slot = ((uint32_t)bt_win[(t >> lg) - win_base] << lg) + (uint32_t)(t & bs_mask);
+            const int64_t row = (int64_t)my_slot * a.num_kv_heads + kvh;
+            cp_async4(tb + 2 * SM::kRows + lane * 4, a.k_scale + row);
+            cp_async4(tb + 2 * SM::kRows + 128 + lane * 4, a.v_scale + row);
         }
-        {
-            const int t = t0 + lane;
-            if (t < t_hi) {
-                const int64_t blk = bt_win[(t >> lg) - win_base];
-                const int64_t row = ((blk << lg) + (t & bs_mask)) * a.num_kv_heads + kvh;
-                cp_async4(tb + 2 * SM::kRows + lane * 4, a.k_scale + row);
-                cp_async4(tb + 2 * SM::kRows + 128 + lane * 4, a.v_scale + row);
+        const int ch = lane % C16;
+#pragma unroll
+        for (int j = 0; j < C16; ++j) {  // rows lane / C16 + (32 / C16) j, chunk lane % C16
+            const int r = lane / C16 + (32 / C16) * j;
+            const uint32_t sl = __shfl_sync(0xFFFFFFFFu, my_slot, r);
+            if (sl != 0xFFFFFFFFu) {
+                const int64_t off = ((int64_t)sl * a.num_kv_heads + kvh) * RB + ch * 16;
+                const uint32_t soff = r * RB + ((ch ^ (r & (C16 - 1))) * 16);
+                cp_async16(tb + soff, reinterpret_cast<const uint8_t*>(a.key_cache) + off);
+                cp_async16(tb + SM::kRows + soff, reinterpret_cast<const uint8_t*>(a.value_cache) + off);
             }
         }
         cp_async_commit();
