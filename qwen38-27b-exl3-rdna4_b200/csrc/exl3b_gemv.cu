@@ -164,13 +164,12 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
         __syncwarp();
         int v = 0;
         if (lane == 0) {
-            // cumulative fence over the warp's partial stores, then the counter; the
-            // second fence orders the reads of other CTAs' partials after it
-            __threadfence();
-            v = atomicAdd(p.counters + Bg, 1);
-            __threadfence();
+            // acq_rel at gpu scope: releases the warp's partial stores (ordered before this by the
+            // __syncwarp) and, for the last arriver, acquires the other CTAs' partials
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(v) : "l"(p.counters + Bg) : "memory");
         }
         v = __shfl_sync(0xFFFFFFFFu, v, 0);
+        __syncwarp();  // every lane's loads of the partials below come after lane 0's acquire
         finalize = (v == cl - cf);
     }
     if (finalize) {
@@ -363,10 +362,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         };
         bool live = true;
         int published = 0;
-        for (int i = 0; live && i < min(nunits, kStages); ++i) live = issue(i);
+        // Only the first two units go out before the wait: every CTA's first unit then arrives
+        // ahead of the rest of the ring instead of queueing behind all CTAs' prefetch.
+        const int early = min(nunits, 2);
+        for (int i = 0; live && i < early; ++i) live = issue(i);
         griddep_wait();  // x may come from the previous kernel
         for (int i = 0; live && i < nunits; ++i) {
-            if (i >= kStages) live = issue(i);
+            if (i >= early) live = issue(i);
             if (!live) break;
             transform(i);
             __syncwarp();
