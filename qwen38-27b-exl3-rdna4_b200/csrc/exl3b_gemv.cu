@@ -40,8 +40,10 @@ constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summ
 constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
 constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
 
-// trellis k-tile rows per unit: about 32 KB of trellis per stage
-__host__ __device__ constexpr int rows_per_unit(int K) { return K <= 2 ? 8 : (K <= 4 ? 4 : 2); }
+// trellis k-tile slots per unit (64 tiles each): 32-64 KB of trellis per stage.  Larger units
+// measured faster than 32 KB ones despite coarser stream-K granularity (fewer unit hand-offs).
+__host__ __device__ constexpr int rows_per_unit(int K) { return K <= 4 ? 8 : 2; }
+constexpr int kMaxUnitRows = 16;  // k-rows of one unit at most (R0 * q), bounding the A_had area
 
 struct GemvGroups {
     const uint16_t* trellis[EXL3B_MAX_GROUPS];
@@ -126,7 +128,7 @@ struct GemvSmem {
     static constexpr int kTile = 32 * K;                  // bytes of one 16x16 tile
     static constexpr int kRowBytes = kSbTiles * kTile;    // stride of the stage slots
     static constexpr int kTrellisStage = R0 * kRowBytes;
-    static constexpr int kAhadStage = 4 * R0 * 8 * MT * 32;  // up to 4 R0 k-tiles x 8 MT rows x 16 halves
+    static constexpr int kAhadStage = (R0 * 4 > kMaxUnitRows ? kMaxUnitRows : R0 * 4) * 8 * MT * 32;  // k-tiles x 8 MT rows x 16 halves
     static constexpr int kStageBytes = kTrellisStage + kAhadStage;
     static constexpr int kAccBytes = 8 * MT * kAccCols * 4;
     static constexpr int kBudget = 220 * 1024;
@@ -597,7 +599,7 @@ static Partition partition(int k, int K, int groups, const int* n) {
     const int kt = k / 16, r0 = rows_per_unit(K);
     Partition q = {};
     for (int qq : {1, 2, 4}) {
-        if (kt % (r0 * qq)) break;  // rows per unit must divide k / 16
+        if (kt % (r0 * qq) || r0 * qq > kMaxUnitRows) break;  // rows per unit must divide k / 16
         Partition t = {};
         t.q = qq;
         t.ku = kt / (r0 * qq);
