@@ -369,19 +369,31 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     int win_base = -1;  // first block index held in bt_win
 
     // ---- Q^T fragments, resident: B[k-slot][n] = Q[row rbase + 8nt + n][dmap], lane (n = g, slots q) ----
+    // The MMAs take the cache values with a bias (int8: 1152 + k, int4: 1024 + nibble), one
+    // instruction cheaper to build than the true values: S^T then carries bias * (sum of the row's q),
+    // removed per score, and O^T carries sum_t P'_t * bias_t, removed at the end (psum).
     uint32_t qb[NT][8][2];
+    float qsum[NT][2];  // sum of the fp16 q of rows 2q and 2q+1 of each n-tile
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         const int r = rbase + 8 * nt + g;
         const __half* qrow = a.q + ((int64_t)(q0 + r / G) * a.num_q_heads + kvh * G + r % G) * kHD;
+        float part = 0.f;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             __half v4[4];
 #pragma unroll
-            for (int s = 0; s < 4; ++s) v4[s] = r < rows ? qrow[Tr::dmap(q, c, s)] : __float2half(0.f);
+            for (int s = 0; s < 4; ++s) {
+                v4[s] = r < rows ? qrow[Tr::dmap(q, c, s)] : __float2half(0.f);
+                part += __half2float(v4[s]);
+            }
             qb[nt][c][0] = h2_as_u32(__halves2half2(v4[0], v4[1]));
             qb[nt][c][1] = h2_as_u32(__halves2half2(v4[2], v4[3]));
         }
+        part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+        part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);  // row g's sum in the four lanes of group g
+        qsum[nt][0] = __shfl_sync(0xFFFFFFFFu, part, 4 * (2 * q));
+        qsum[nt][1] = __shfl_sync(0xFFFFFFFFu, part, 4 * (2 * q + 1));
     }
 
     // ---- tile loader: all of a 32-token tile's rows and scales, one cp.async group ----
@@ -427,7 +439,8 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     };
 
     const float sl2 = a.score_scale * 1.4426950408889634f;  // scores in the log2 domain
-    float m_i[NT][2], l_i[NT][2], lim[NT][2];
+    // l_i and psum hold this lane's share (its tokens); they are summed over the lane group at the end
+    float m_i[NT][2], l_i[NT][2], lim[NT][2], psum[NT][2];
     float acc[NT][8][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -435,6 +448,7 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         for (int h = 0; h < 2; ++h) {
             m_i[nt][h] = -INFINITY;
             l_i[nt][h] = 0.f;
+            psum[nt][h] = 0.f;
             // causal limit of row 2q + h: key t allowed if t <= L - qlen + query index
             const int r = rbase + 8 * nt + 2 * q + h;
             lim[nt][h] = (r < rows) ? (float)(L - qlen + r / G) : -1.f;
@@ -472,9 +486,13 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         // this tile holds exact rows only if it meets the first kSinks or the last kTail positions
         const bool ex_tile = has_exact && (t0 < kSinks || t0 + 31 >= L - kTail);
 
-        // K fragments of token r of the tile: k-slot pairs (2q, 2q+1) -> kf[c][0], (2q+8, 2q+9) -> kf[c][1]
-        auto k_frag = [&](int r, uint32_t (&kf)[8][2]) -> float {
+        // tiles without exact rows run on biased values (see qsum); the others on true values
+        const bool biased = !ex_tile;
+        // K fragments of token r of the tile: k-slot pairs (2q, 2q+1) -> kf[c][0], (2q+8, 2q+9) -> kf[c][1];
+        // returns the token's k scale, and its bias in kb
+        auto k_frag = [&](int r, uint32_t (&kf)[8][2], float& kb) -> float {
             const int t = t0 + r;
+            kb = 0.f;
             if (t >= t_hi) {
 #pragma unroll
                 for (int c = 0; c < 8; ++c) kf[c][0] = kf[c][1] = 0u;
@@ -496,18 +514,32 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
                 const uint4 w0 = chunk_at(0, r, 2 * q), w1 = chunk_at(0, r, 2 * q + 1);
                 const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-                for (int c = 0; c < 8; ++c) i8x4_to_h2(w[c], kf[c][0], kf[c][1]);
+                for (int c = 0; c < 8; ++c) {  // 1152 + k, exact in fp16
+                    const uint32_t u = w[c] ^ 0x80808080u;
+                    kf[c][0] = prmt(u, 0x64646464u, 0x5140u);
+                    kf[c][1] = prmt(u, 0x64646464u, 0x7362u);
+                }
+                kb = 1152.f;
                 return ksc_s[r];
             } else {
                 const uint4 w4 = chunk_at(0, r, q);
                 const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
                 const uint32_t sb = __float_as_uint(ksc_s[r]);
-                const uint32_t zp = 0x6400u | (sb & 0xFu);
-                const uint32_t zp2 = zp | (zp << 16);
+                if (biased) {
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    kf[c][0] = nib_pair(w[c / 2], 2 * (c % 2), zp2);
-                    kf[c][1] = nib_pair(w[c / 2], 2 * (c % 2) + 1, zp2);
+                    for (int c = 0; c < 8; ++c) {  // 1024 + nibble
+                        kf[c][0] = ((w[c / 2] >> (4 * (2 * (c % 2)))) & 0x000F000Fu) | 0x64006400u;
+                        kf[c][1] = ((w[c / 2] >> (4 * (2 * (c % 2) + 1))) & 0x000F000Fu) | 0x64006400u;
+                    }
+                    kb = 1024.f + (float)(sb & 0xFu);
+                } else {
+                    const uint32_t zp = 0x6400u | (sb & 0xFu);
+                    const uint32_t zp2 = zp | (zp << 16);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        kf[c][0] = nib_pair(w[c / 2], 2 * (c % 2), zp2);
+                        kf[c][1] = nib_pair(w[c / 2], 2 * (c % 2) + 1, zp2);
+                    }
                 }
                 return __uint_as_float(sb & 0xFFFFFFF0u);
             }
@@ -516,12 +548,12 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         // ---------------- S^T = K Q^T: two m-tiles of 16 tokens ----------------
         // s[nt][mt][e]: token 16mt + g + 8(e >> 1), row 2q + (e & 1) of n-tile nt
         float s[NT][2][4];
-        float ksc[2][2];
+        float ksc[2][2], kbias[2][2];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
             uint32_t kA[8][2], kB[8][2];
-            ksc[mt][0] = k_frag(16 * mt + g, kA);
-            ksc[mt][1] = k_frag(16 * mt + g + 8, kB);
+            ksc[mt][0] = k_frag(16 * mt + g, kA, kbias[mt][0]);
+            ksc[mt][1] = k_frag(16 * mt + g + 8, kB, kbias[mt][1]);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 float d4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -541,7 +573,7 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    float v = s[nt][mt][e] * (sl2 * ksc[mt][e >> 1]);
+                    float v = fmaf(-kbias[mt][e >> 1], qsum[nt][e & 1], s[nt][mt][e]) * (sl2 * ksc[mt][e >> 1]);
                     if (masked) {
                         const int t = t0 + 16 * mt + g + 8 * (e >> 1);
                         v = (t < t_hi && (float)t <= lim[nt][e & 1]) ? v : -INFINITY;
@@ -581,11 +613,8 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                float v = rsum[nt][h];
-                v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
-                v += __shfl_xor_sync(0xFFFFFFFFu, v, 8);
-                v += __shfl_xor_sync(0xFFFFFFFFu, v, 16);
-                l_i[nt][h] = l_i[nt][h] * corr[nt][h] + v;
+                l_i[nt][h] = l_i[nt][h] * corr[nt][h] + rsum[nt][h];
+                psum[nt][h] *= corr[nt][h];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     acc[nt][j][h] *= corr[nt][h];
@@ -611,11 +640,28 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
                     }
                 }
             }
+            // bias of the V values the MMA will see for tokens rA, rB (0 on the exact-row path)
+            float wA = 0.f, wB = 0.f;
+            if (biased) {
+                const int rA = 16 * kc + g, rB = rA + 8;
+                if (KV == 8) {
+                    wA = (t0 + rA < t_hi) ? 1152.f : 0.f;
+                    wB = (t0 + rB < t_hi) ? 1152.f : 0.f;
+                } else {
+                    wA = (t0 + rA < t_hi) ? 1024.f + (float)(__float_as_uint(vsc_s[rA]) & 0xFu) : 0.f;
+                    wB = (t0 + rB < t_hi) ? 1024.f + (float)(__float_as_uint(vsc_s[rB]) & 0xFu) : 0.f;
+                }
+            }
             uint32_t pb[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                pb[nt][0] = movm_t(h2_as_u32(__floats2half2_rn(s[nt][kc][0] * vsA, s[nt][kc][1] * vsA)));
-                pb[nt][1] = movm_t(h2_as_u32(__floats2half2_rn(s[nt][kc][2] * vsB, s[nt][kc][3] * vsB)));
+                const __half2 lo = __floats2half2_rn(s[nt][kc][0] * vsA, s[nt][kc][1] * vsA);
+                const __half2 hi = __floats2half2_rn(s[nt][kc][2] * vsB, s[nt][kc][3] * vsB);
+                pb[nt][0] = movm_t(h2_as_u32(lo));
+                pb[nt][1] = movm_t(h2_as_u32(hi));
+                // the exact fp16 P' the MMA multiplies, weighted by each token's bias
+                psum[nt][0] = fmaf(__low2float(hi), wB, fmaf(__low2float(lo), wA, psum[nt][0]));
+                psum[nt][1] = fmaf(__high2float(hi), wB, fmaf(__high2float(lo), wA, psum[nt][1]));
             }
             // V^T A fragments: tokens T0..T3 = 16kc + (2q, 2q+1, 2q+8, 2q+9); m-tile j rows g / g+8 are
             // d = 16g + 2j / 16g + 2j + 1.  va[j][0..3] = (a0, a1, a2, a3)
@@ -633,19 +679,18 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
                         w[T][0] = v4.x ^ 0x80808080u; w[T][1] = v4.y ^ 0x80808080u;
                         w[T][2] = v4.z ^ 0x80808080u; w[T][3] = v4.w ^ 0x80808080u;
                     }
-                    const __half2 off = u32_as_h2(0x64806480u);  // 1152
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
+                    for (int j = 0; j < 8; ++j) {  // 1152 + v, exact in fp16
                         const uint32_t sel = (j & 1) ? 0x7362u : 0x5140u;
 #pragma unroll
                         for (int pr = 0; pr < 2; ++pr) {  // token pairs (T0, T1) and (T2, T3)
                             const uint32_t x = prmt(w[2 * pr][j >> 1], w[2 * pr + 1][j >> 1], sel);
-                            va[j][2 * pr] = h2_as_u32(__hsub2(u32_as_h2(prmt(x, 0x64646464u, 0x5140u)), off));
-                            va[j][2 * pr + 1] = h2_as_u32(__hsub2(u32_as_h2(prmt(x, 0x64646464u, 0x7362u)), off));
+                            va[j][2 * pr] = prmt(x, 0x64646464u, 0x5140u);
+                            va[j][2 * pr + 1] = prmt(x, 0x64646464u, 0x7362u);
                         }
                     }
                 } else {
-                    uint32_t w[4][2], zpp[2];
+                    uint32_t w[4][2];
 #pragma unroll
                     for (int T = 0; T < 4; ++T) {
                         uint4 v4 = make_uint4(0u, 0u, 0u, 0u);
@@ -654,26 +699,18 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
                         w[T][1] = (g & 1) ? v4.w : v4.y;
                     }
 #pragma unroll
-                    for (int pr = 0; pr < 2; ++pr) {
-                        const int rA = rT[2 * pr], rB = rT[2 * pr + 1];
-                        const uint32_t za = (t0 + rA < t_hi) ? (__float_as_uint(vsc_s[rA]) & 0xFu) : 0u;
-                        const uint32_t zb = (t0 + rB < t_hi) ? (__float_as_uint(vsc_s[rB]) & 0xFu) : 0u;
-                        zpp[pr] = (0x6400u | za) | ((0x6400u | zb) << 16);
-                    }
-#pragma unroll
                     for (int i = 0; i < 2; ++i)
 #pragma unroll
                         for (int kk = 0; kk < 4; kk += 2) {  // bytes (kk, kk+1) of word i -> m-tiles 4i+kk, 4i+kk+1
                             const uint32_t sel = kk ? 0x7362u : 0x5140u;
 #pragma unroll
-                            for (int pr = 0; pr < 2; ++pr) {
+                            for (int pr = 0; pr < 2; ++pr) {  // 1024 + nibble
                                 const uint32_t x = prmt(w[2 * pr][i], w[2 * pr + 1][i], sel);
                                 const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
-                                const __half2 z = u32_as_h2(zpp[pr]);
-                                va[4 * i + kk][2 * pr] = h2_as_u32(__hsub2(u32_as_h2(prmt(lo, 0x64646464u, 0x5140u)), z));
-                                va[4 * i + kk][2 * pr + 1] = h2_as_u32(__hsub2(u32_as_h2(prmt(hi, 0x64646464u, 0x5140u)), z));
-                                va[4 * i + kk + 1][2 * pr] = h2_as_u32(__hsub2(u32_as_h2(prmt(lo, 0x64646464u, 0x7362u)), z));
-                                va[4 * i + kk + 1][2 * pr + 1] = h2_as_u32(__hsub2(u32_as_h2(prmt(hi, 0x64646464u, 0x7362u)), z));
+                                va[4 * i + kk][2 * pr] = prmt(lo, 0x64646464u, 0x5140u);
+                                va[4 * i + kk][2 * pr + 1] = prmt(hi, 0x64646464u, 0x5140u);
+                                va[4 * i + kk + 1][2 * pr] = prmt(lo, 0x64646464u, 0x7362u);
+                                va[4 * i + kk + 1][2 * pr + 1] = prmt(hi, 0x64646464u, 0x7362u);
                             }
                         }
                 }
@@ -724,6 +761,25 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         __syncwarp();  // the ring slot of this tile is refilled next iteration
     }
     cp_async_wait<0>();
+
+    // lane shares of l and of the bias sums -> row totals (the lanes of a row differ in g)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float l = l_i[nt][h], ps = psum[nt][h];
+#pragma unroll
+            for (int d = 4; d <= 16; d <<= 1) {
+                l += __shfl_xor_sync(0xFFFFFFFFu, l, d);
+                ps += __shfl_xor_sync(0xFFFFFFFFu, ps, d);
+            }
+            l_i[nt][h] = l;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                acc[nt][j][h] -= ps;
+                acc[nt][j][2 + h] -= ps;
+            }
+        }
 
     // ---- partial of this split: acc (d order restored), m, l ----
     // acc[nt][j][h] is (d = 16g + 2j, row 2q + h), acc[nt][j][2 + h] is (d = 16g + 2j + 1, row 2q + h)
