@@ -469,7 +469,12 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         return a.exact_tag[(int64_t)rs * kExactRows + e] == t ? e : -1;
     };
 
-    for (int ti = 0; ti < SM::kRing - 1 && ti < ntiles; ++ti) issue_tile(ti);
+    // exactly kRing - 1 groups ahead of the loop (empty ones for splits shorter than that), so that
+    // wait_group<kRing - 1> in the loop always means "tile ti has landed"
+    for (int ti = 0; ti < SM::kRing - 1; ++ti) {
+        if (ti < ntiles) issue_tile(ti);
+        else cp_async_commit();
+    }
 
     for (int ti = 0; ti < ntiles; ++ti) {
         if (ti + SM::kRing - 1 < ntiles) issue_tile(ti + SM::kRing - 1);
