@@ -315,6 +315,69 @@ def bench_prefill(torch, dev, K: int, m: int = 2048, iters: int = 5) -> dict:
             "route": "had128 + dequant to fp16 + dense fp16 GEMM (torch.mm) + had128"}
 
 
+def bench_decode(torch, dev, steps: int, warmup: int, ctx: int = 32768,
+                 cases=((1, 1), (8, 1), (1, 4))) -> list:
+    """Decode tokens/s of the synthetic 64-layer 27B-class decoder (exl3rocm.synthetic) with an int8
+    paged KV cache of ctx tokens per sequence: (batch, q_len) = (1, 1) and (8, 1) decode, (1, 4) a
+    4-token speculative verify.  Each step is one CUDA-graph replay of embed -> 64 layers -> lm_head
+    -> argmax, fed the previous step's tokens on the device; timed with CUDA events over `steps`
+    replays after `warmup`.  e2e adds, every step, the input tokens from pinned host memory and the
+    output tokens back to it.  Weights (9.5 GB) and caches exceed L2 many times over."""
+    from exl3rocm.synthetic import DecoderShape, SyntheticDecoder
+    shape = DecoderShape()
+    out, base = [], None
+    for batch, q_len in cases:
+        dec = SyntheticDecoder(shape, dev, batch=batch, q_len=q_len, ctx=ctx, seed=2024, weights_of=base)
+        base = base or dec
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        dec.reserve(st)
+        tokens = torch.randint(0, shape.vocab, (dec.M,), device=dev)
+        with torch.cuda.stream(st):
+            dec.step(tokens)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                dec.step(tokens)
+                tokens.copy_(dec.next_tokens)  # next step's input, on the device
+            for _ in range(warmup):
+                graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            for _ in range(steps):
+                graph.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        # end to end: host tokens in, host tokens out, every step
+        t_host = torch.randint(0, shape.vocab, (dec.M,), dtype=torch.int64).pin_memory()
+        o_host = torch.empty(dec.M, dtype=torch.int64).pin_memory()
+        with torch.cuda.stream(st):
+            e0.record(st)
+            for _ in range(steps):
+                tokens.copy_(t_host, non_blocking=True)
+                graph.replay()
+                o_host.copy_(dec.next_tokens, non_blocking=True)
+            e1.record(st)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / steps
+        wb, kb = dec.weight_bytes(), dec.kv_bytes()
+        out.append({"batch": batch, "q_len": q_len, "ctx": ctx, "ms_per_step": ms,
+                    "tok_s": batch / (ms * 1e-3) if q_len == 1 else None,
+                    "rows_per_s": dec.M / (ms * 1e-3), "e2e_ms_per_step": e2e_ms,
+                    "e2e_tok_s": batch / (e2e_ms * 1e-3) if q_len == 1 else None,
+                    "weight_bytes": wb, "kv_bytes": kb, "gb_s": (wb + kb) / (ms * 1e-3) / 1e9,
+                    "gpu_launches_per_step": dec.launches_per_step()})
+        del graph
+        if dec is not base:
+            del dec
+        torch.cuda.empty_cache()
+    del base
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------------------------
 # main
 # ---------------------------------------------------------------------------------------------
@@ -327,7 +390,8 @@ def main():
     ap.add_argument("--bits", type=int, default=4)
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--no-extra", action="store_true", help="skip the KV-attention and prefill legs")
+    ap.add_argument("--no-extra", action="store_true", help="skip the KV-attention, prefill and decode legs")
+    ap.add_argument("--no-decode", action="store_true", help="skip the whole-model decode tok/s leg")
     ap.add_argument("--tp-reduce", default="fused", choices=["fused", "nccl"],
                     help="row-parallel reduction under --gpus > 1: inside the GEMV kernel over peer memory, "
                          "or an NCCL all-reduce after it")
@@ -480,7 +544,7 @@ def main():
     achieved = gu_bytes / (gu_ms_med * 1e-3) / 1e9
     # DRAM bytes (read + write) of one gemv_kernel launch of this call, from the ncu capture
     # summarised in profiles/gemv_kernel_gate_up_m1_k4.md (measured for K = 4, m = 1 only)
-    traffic = (89.291264e6 + 3.387904e6) if (K == 4 and M == 1 and world == 1) else None
+    traffic = (89.314304e6 + 3.256320e6) if (K == 4 and M == 1 and world == 1) else None
 
     # ---- end to end: pinned host x -> device, the layer's ops (graph), y -> pinned host ----
     x_host = torch.randn((M, HIDDEN), dtype=torch.float32).to(torch.bfloat16).pin_memory()
@@ -510,6 +574,10 @@ def main():
                                  for kind, ctx, b, ql in ((8, 32768, 8, 1), (4, 32768, 8, 1), (8, 32768, 1, 4),
                                                           (4, 65536, 1, 1), (8, 4096, 8, 1))]
         extra["prefill_m2048"] = bench_prefill(torch, dev, K)
+        if not args.no_decode:
+            del layers, outs, inputs
+            torch.cuda.empty_cache()
+            extra["decode"] = bench_decode(torch, dev, steps=max(10, args.steps), warmup=args.warmup)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

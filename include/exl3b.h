@@ -45,6 +45,16 @@ extern "C" {
 /* or-ed into the codebook argument of the m <= 16 linears: x is bf16 and is rounded to fp16 inside
  * the kernel, exactly as the reference's x.to(float16) at the op boundary (ops.py:72-73) */
 #define EXL3B_X_BF16 0x100
+/* Epilogue flags (or-ed into `codebook` of exl3b_linear / exl3b_linear_grouped / exl3b_linear_tp;
+ * no reference counterpart: the reference runs these as separate vLLM ops, and its own analysis of
+ * fusing them is docs/EFFICIENCY_INVESTIGATION.md:36-66).
+ *   EXL3B_ACT_SILU_MUL: exl3b_linear_grouped with exactly two groups of equal width (gate, up):
+ *     y[0][m][n] = fp16( fp16(silu(gate)) * up ), gate/up being the two groups' fp16 outputs;
+ *     the roundings of torch's fp16 F.silu(gate) * up (vLLM SiluAndMul).  y[1] is not written.
+ *   EXL3B_Y_ADD: y = fp16(y + result), one fp16 add per element (the residual add); y must hold
+ *     the residual before the call.  Not combinable with EXL3B_ACT_SILU_MUL. */
+#define EXL3B_ACT_SILU_MUL 0x200
+#define EXL3B_Y_ADD 0x400
 
 #define EXL3B_MAX_GROUPS 8
 #define EXL3B_GEMV_MAX_ROWS 16
@@ -244,6 +254,32 @@ EXL3B_API int exl3b_linear_tp(const uint16_t* x, int m, int k, const uint16_t* t
 /* Reads the kernel error word of a linear workspace (0 = none; otherwise the code of a wait that
  * gave up) into *out, synchronising `stream`.  Test and diagnostics helper. */
 EXL3B_API int exl3b_linear_workspace_error(const void* workspace, int* out, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Decoder-layer glue between the linears and the attention.  The reference leaves these steps to
+ * vLLM's own kernels (its plugin replaces only the linears and the KV cache); they are here so a
+ * decode step runs on this library alone.  fp16 rows with strides in elements.
+ * ------------------------------------------------------------------------------------------ */
+
+/* RMSNorm of `rows` rows of `cols` (cols % 8 == 0, <= 16384).  residual != NULL: residual =
+ * fp16(x + residual) first, and that sum is normalised (vLLM fused_add_rms_norm); otherwise x is
+ * (vLLM rms_norm).  out = fp16( fp16(v * rsqrt(mean(v^2) + eps)) * weight ), mean in fp32. */
+EXL3B_API int exl3b_rmsnorm(const uint16_t* x, int64_t ldx, uint16_t* residual, int64_t ldr, const uint16_t* weight,
+                            uint16_t* out, int64_t ldo, int rows, int cols, float eps, void* stream);
+
+/* Neox rotary embedding, head size 128 (vLLM get_rope(..., is_neox_style=True)).  Row t of qkv
+ * (stride ld) holds num_q_heads q heads then num_k_heads k heads; q is written rotated to q_out
+ * (stride ld_q), k is rotated in place.  cos_sin fp32 [max_position][128]: cos of the 64
+ * frequencies, then their sin.  positions int64 [tokens]; a position outside [0, max_position)
+ * leaves the token's k as it was and writes zeros for its q. */
+EXL3B_API int exl3b_rope_neox(uint16_t* qkv, int64_t ld, uint16_t* q_out, int64_t ld_q, int tokens, int num_q_heads,
+                              int num_k_heads, const int64_t* positions, const float* cos_sin, int64_t max_position,
+                              void* stream);
+
+/* SiluAndMul: out[r][c] = fp16( fp16(silu(in[r][c])) * in[r][n + c] ), n % 8 == 0 (the
+ * activation of EXL3B_ACT_SILU_MUL, for rows taken by the dequantise + GEMM route). */
+EXL3B_API int exl3b_silu_mul(const uint16_t* in, int64_t ld_in, uint16_t* out, int64_t ld_out, int rows, int n,
+                             void* stream);
 
 #ifdef __cplusplus
 }

@@ -47,6 +47,14 @@ EXL3B_DEV uint32_t cb_hash(uint32_t w) {
 EXL3B_DEV uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 EXL3B_DEV __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
+// silu(g) * u with the roundings of torch's fp16 F.silu(g) * u (vLLM SiluAndMul.forward_native):
+// silu = g / (1 + exp(-g)) in fp32 rounded to fp16, then one fp16 multiply
+EXL3B_DEV __half2 silu_mul2(__half2 g, __half2 u) {
+    const float a = __low2float(g), b = __high2float(g);
+    const __half2 s = __floats2half2_rn(a / (1.0f + expf(-a)), b / (1.0f + expf(-b)));
+    return __hmul2(s, u);
+}
+
 // Two 16-bit states -> packed half2 (first state in the low half).
 // cb2: fp16_fma(fp16(0x6400 + bytesum(w*M)), k_inv, k_bias), one rounding (fma.rn.f16x2).
 // cb0/cb1: lop3 then fp16 add of the two halves of each hashed word, one rounding.

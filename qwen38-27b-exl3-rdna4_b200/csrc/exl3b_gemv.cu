@@ -70,10 +70,17 @@ struct GemvParams {
     int units, ctas;
     int sb_cols;          // widest super-block of the call, in columns
     int64_t ldy;
+    int y_add;            // y += result (the residual add of the caller's block)
+    // SwiGLU epilogue (act): groups 0 and 1 (gate, up) of equal width stage their fp16 outputs in
+    // `stage` [m][2n]; the second finisher of column block b writes silu(gate) * up to y[0]
+    int act;
+    __half* stage;
+    int act_ctr;          // first pair counter (after the per-block counters of the call)
     // fused tensor-parallel all-reduce (tp_size > 1): every rank's communication buffer
     int tp_size, tp_rank, tp_blocks, tp_rows;
     uint8_t* tp_buf[EXL3B_MAX_TP];
 };
+
 
 // Communication buffer of one rank: a 256-byte header (call counter, finished-CTA counter), then
 // slots [2 parities][tp ranks][blocks][rows][128] of (fp32 value, call number) pairs, 8 bytes each.
@@ -207,14 +214,49 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
             __half2 y23 = __floats2half2_rn(h[2] * kRScale, h[3] * kRScale);
             y01 = __hmul2(y01, u32_as_h2(sv.x));
             y23 = __hmul2(y23, u32_as_h2(sv.y));
-            *reinterpret_cast<uint2*>(p.g.y[si.g] + row * p.ldy + b * 128 + 4 * lane) =
-                make_uint2(h2_as_u32(y01), h2_as_u32(y23));
+            if (p.act) {  // staged in L2 for the pair's second finisher
+                __stcg(reinterpret_cast<uint2*>(p.stage + (int64_t)row * 2 * (p.g.n_tiles[0] * 16) +
+                                                si.g * (p.g.n_tiles[0] * 16) + b * 128 + 4 * lane),
+                       make_uint2(h2_as_u32(y01), h2_as_u32(y23)));
+                return;
+            }
+            uint2* dst = reinterpret_cast<uint2*>(p.g.y[si.g] + row * p.ldy + b * 128 + 4 * lane);
+            if (p.y_add) {  // one fp16 add (exact sum, one rounding), as torch's fp16 x + residual
+                const uint2 o = *dst;
+                y01 = __hadd2(y01, u32_as_h2(o.x));
+                y23 = __hadd2(y23, u32_as_h2(o.y));
+            }
+            *dst = make_uint2(h2_as_u32(y01), h2_as_u32(y23));
         };
         if (p.tp_size <= 1) {
             for (int row = 0; row < m; ++row) {
                 float v[4];
                 block_sum(row, v);
                 finish_row(row, v);
+            }
+            if (p.act) {
+                // gate and up block b are finished by different warps, in any order: the second
+                // one (pair counter) reads both staged blocks and writes the activation
+                __syncwarp();
+                int w = 0;
+                if (lane == 0)
+                    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n"
+                                 : "=r"(w) : "l"(p.counters + p.act_ctr + b) : "memory");
+                w = __shfl_sync(0xFFFFFFFFu, w, 0);
+                __syncwarp();
+                if (w == 1) {
+                    const int64_t nn = p.g.n_tiles[0] * 16;
+                    for (int row = 0; row < m; ++row) {
+                        const __half* s = p.stage + (int64_t)row * 2 * nn + b * 128 + 4 * lane;
+                        const uint2 g = __ldcg(reinterpret_cast<const uint2*>(s));
+                        const uint2 u = __ldcg(reinterpret_cast<const uint2*>(s + nn));
+                        const __half2 a01 = silu_mul2(u32_as_h2(g.x), u32_as_h2(u.x));
+                        const __half2 a23 = silu_mul2(u32_as_h2(g.y), u32_as_h2(u.y));
+                        *reinterpret_cast<uint2*>(p.g.y[0] + row * p.ldy + b * 128 + 4 * lane) =
+                            make_uint2(h2_as_u32(a01), h2_as_u32(a23));
+                    }
+                    if (lane == 0) p.counters[p.act_ctr + b] = 0;
+                }
             }
         } else {
             // Exchange this rank's k-slice partial of block b with every rank: (value, call) pairs
@@ -620,14 +662,16 @@ static Partition partition(int k, int K, int groups, const int* n) {
 }
 
 struct WsLayout {
-    size_t counters, partials, total;
+    size_t counters, partials, stage, total;
 };
 
-static WsLayout ws_layout(int m, int k, int groups, const Partition& q) {
+// stage_cols: columns of the SwiGLU staging area (both groups), 0 without the activation
+static WsLayout ws_layout(int m, int k, int groups, const Partition& q, int64_t stage_cols) {
     WsLayout L;
     L.counters = kHeaderBytes;
     L.partials = round_up(L.counters + kCounterBytes, 256);
-    L.total = round_up(L.partials + (size_t)(q.ctas + q.super_blocks - 1) * m * q.sb_cols * 4, 256);
+    L.stage = round_up(L.partials + (size_t)(q.ctas + q.super_blocks - 1) * m * q.sb_cols * 4, 256);
+    L.total = round_up(L.stage + (size_t)m * stage_cols * 2, 256);
     return L;
 }
 
@@ -674,8 +718,11 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
                 int K, int codebook, const uint16_t* const* suh, const uint16_t* const* svh, uint16_t* const* y,
                 int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm) {
     const bool x_bf16 = (codebook & EXL3B_X_BF16) != 0;
-    codebook &= ~EXL3B_X_BF16;
+    const bool act = (codebook & EXL3B_ACT_SILU_MUL) != 0;
+    const bool y_add = (codebook & EXL3B_Y_ADD) != 0;
+    codebook &= ~(EXL3B_X_BF16 | EXL3B_ACT_SILU_MUL | EXL3B_Y_ADD);
     if (K < 1 || K > 8 || codebook < 0 || codebook > 2) return EXL3B_DECLINED;
+    if (act && (groups != 2 || !n || n[0] != n[1] || comm || y_add)) return EXL3B_DECLINED;
     if (m < 1 || m > EXL3B_GEMV_MAX_ROWS || groups < 1 || groups > EXL3B_MAX_GROUPS) return EXL3B_DECLINED;
     if (k <= 0 || k % 128) return EXL3B_DECLINED;
     if (!x || !trellis || !n || !suh || !svh || !y || !workspace) return EXL3B_BAD_ARG;
@@ -684,12 +731,14 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     for (int g = 0; g < groups; ++g) {
         if (n[g] <= 0 || n[g] % 128) return EXL3B_DECLINED;
         if (ldy < n[g]) return EXL3B_BAD_ARG;
-        if (!trellis[g] || !suh[g] || !svh[g] || !y[g]) return EXL3B_BAD_ARG;
-        if (!aligned(trellis[g], 16) || !aligned(suh[g], 8) || !aligned(svh[g], 8) || !aligned(y[g], 8))
+        const uint16_t* yg = act ? y[0] : y[g];  // the activation has one output
+        if (!trellis[g] || !suh[g] || !svh[g] || !yg) return EXL3B_BAD_ARG;
+        if (!aligned(trellis[g], 16) || !aligned(suh[g], 8) || !aligned(svh[g], 8) || !aligned(yg, 8))
             return EXL3B_BAD_ARG;
         n_total += n[g];
     }
-    if (n_total / 128 > kMaxBlocks) return EXL3B_DECLINED;
+    // per-block counters, then (act) one pair counter per column block of a group
+    if ((n_total + (act ? n[0] : 0)) / 128 > kMaxBlocks) return EXL3B_DECLINED;
     if (comm) {
         if (groups != 1 || comm->tp_size < 2 || comm->tp_size > EXL3B_MAX_TP || comm->tp_rank < 0 ||
             comm->tp_rank >= comm->tp_size || n[0] / 128 > comm->max_blocks || m > comm->max_rows)
@@ -698,7 +747,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
             if (!comm->buffers[r] || !aligned(comm->buffers[r], 256)) return EXL3B_BAD_ARG;
     }
     const Partition q = partition(k, K, groups, n);
-    const WsLayout L = ws_layout(m, k, groups, q);
+    const WsLayout L = ws_layout(m, k, groups, q, act ? n_total : 0);
     if (ws_bytes < L.total) return EXL3B_WORKSPACE;
 
     cudaStream_t st = (cudaStream_t)stream;
@@ -710,7 +759,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
         p.suh[g] = reinterpret_cast<const __half*>(suh[g]);
         p.g.trellis[g] = trellis[g];
         p.g.svh[g] = reinterpret_cast<const __half*>(svh[g]);
-        p.g.y[g] = reinterpret_cast<__half*>(y[g]);
+        p.g.y[g] = reinterpret_cast<__half*>(act ? y[0] : y[g]);
         p.g.n_tiles[g] = n[g] / 16;
         p.g.blk_prefix[g] = blk;
         p.g.sb_prefix[g] = sbs;
@@ -738,6 +787,10 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     p.ctas = q.ctas;
     p.sb_cols = q.sb_cols;
     p.ldy = ldy;
+    p.y_add = y_add ? 1 : 0;
+    p.act = act ? 1 : 0;
+    p.stage = reinterpret_cast<__half*>(ws + L.stage);
+    p.act_ctr = blk;
     p.tp_size = comm ? comm->tp_size : 1;
     if (comm) {
         p.tp_rank = comm->tp_rank;
@@ -768,7 +821,8 @@ extern "C" size_t exl3b_linear_workspace_bytes(int m, int k, int groups, int64_t
     q.super_blocks = (int)std::min<int64_t>(blocks, (blocks + 1) / 2 + groups - 1);  // q = 4: 2 blocks each
     q.sb_cols = (int)std::min<int64_t>(blocks, 8) * 128;
     q.ctas = (int)std::min<int64_t>(num_sms(), (int64_t)q.super_blocks * ((k / 16) / rows_per_unit(8)));
-    return ws_layout(m, k, groups, q).total;
+    // two groups may carry the SwiGLU epilogue, which stages both outputs
+    return ws_layout(m, k, groups, q, groups == 2 ? n_total : 0).total;
 }
 
 extern "C" int exl3b_linear(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K, int codebook,

@@ -934,8 +934,9 @@ static int kv_num_sms() {
 }
 
 static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len) {
-    // twelve single-warp CTAs per SM fit (registers and shared memory): fill them
-    const int want = (12 * kv_num_sms() + num_seqs * num_kv_heads - 1) / (num_seqs * num_kv_heads);
+    // twelve single-warp CTAs per SM fit (registers and shared memory): fill them in one wave
+    // (rounded down: a few CTAs more than the slots would run as a second, almost empty wave)
+    const int want = (12 * kv_num_sms()) / (num_seqs * num_kv_heads);
     const int by_len = (max_seq_len + 63) / 64;
     return std::max(1, std::min(kMaxSplits, std::min(want, by_len)));
 }

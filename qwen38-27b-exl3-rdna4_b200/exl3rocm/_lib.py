@@ -62,6 +62,9 @@ SIGNATURES = {
                                  i32, i32, i32, f32, c_vp, sz, c_vp]),
     "exl3b_kv_int4_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,
                                  i32, i32, i32, f32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, sz, c_vp]),
+    "exl3b_rmsnorm": (i32, [c_vp, i64, c_vp, i64, c_vp, c_vp, i64, i32, i32, f32, c_vp]),
+    "exl3b_rope_neox": (i32, [c_vp, i64, c_vp, i64, i32, i32, i32, c_vp, c_vp, i64, c_vp]),
+    "exl3b_silu_mul": (i32, [c_vp, i64, c_vp, i64, i32, i32, c_vp]),
 }
 
 _lib = None

@@ -22,6 +22,8 @@ from . import _lib
 GEMV_MAX_ROWS = 16
 MAX_GROUPS = 8
 X_BF16 = 0x100  # EXL3B_X_BF16: x is bf16, rounded to fp16 inside the kernel
+ACT_SILU_MUL = 0x200  # EXL3B_ACT_SILU_MUL: two groups (gate, up) -> fp16(fp16(silu(gate)) * up)
+Y_ADD = 0x400  # EXL3B_Y_ADD: y = fp16(y + result), the residual add in the epilogue
 RECON_SLICE_N = 17408  # widest model layer, as the reference (ops.py:22-24)
 
 _ws: dict = {}    # (device index, stream handle) -> uint8 workspace (counters zeroed once)
@@ -126,15 +128,23 @@ def had_r_128(inp: torch.Tensor, out: torch.Tensor, pre: Optional[torch.Tensor],
 
 
 def linear_into(x2: torch.Tensor, trellis: list, suh: list, svh: list, K: int, mcg: bool, mul1: bool,
-                y: torch.Tensor) -> None:
+                y: torch.Tensor, flags: int = 0) -> None:
     """Fused M <= 16 linear of groups sharing x and K; group i -> its column slice of y.  x2 is fp16,
-    or bf16 (rounded to fp16 inside the kernel, as the reference's cast at the op boundary)."""
+    or bf16 (rounded to fp16 inside the kernel, as the reference's cast at the op boundary).
+    flags: Y_ADD (y += result) or ACT_SILU_MUL (two groups; y receives the activation)."""
     M, k = x2.shape
     ng = len(trellis)
     widths = [int(s.shape[0]) for s in svh]
     ws = reserve_workspace(x2.device, k, sum(widths), ng, max(M, 1))
     st = _stream(x2.device)
-    cb = _cb(mcg, mul1) | (X_BF16 if x2.dtype == torch.bfloat16 else 0)
+    cb = _cb(mcg, mul1) | (X_BF16 if x2.dtype == torch.bfloat16 else 0) | flags
+    if flags & ACT_SILU_MUL:
+        assert ng == 2 and widths[0] == widths[1] and y.shape[1] == widths[0]
+        vp = _lib.c_vp * 2
+        _lib.call("exl3b_linear_grouped", x2.data_ptr(), M, k, 2, vp(*[t.data_ptr() for t in trellis]),
+                  (_lib.i32 * 2)(*widths), K, cb, vp(*[s.data_ptr() for s in suh]), vp(*[s.data_ptr() for s in svh]),
+                  vp(y.data_ptr(), y.data_ptr()), y.stride(0), ws.data_ptr(), ws.numel(), st)
+        return
     if ng == 1:
         _lib.call("exl3b_linear", x2.data_ptr(), M, k, trellis[0].data_ptr(), widths[0], K, cb,
                   suh[0].data_ptr(), svh[0].data_ptr(), y.data_ptr(), y.stride(0), ws.data_ptr(), ws.numel(), st)
@@ -240,3 +250,65 @@ def exl3_linear_groups(x: torch.Tensor, trellis: list[torch.Tensor], suh: list[t
 @exl3_linear_groups.register_fake
 def _(x, trellis, suh, svh, K, mcg, mul1, ptrs_trellis=None, ptrs_suh=None, ptrs_svh=None):
     return x.new_empty((*x.shape[:-1], sum(s.shape[0] for s in svh)), dtype=torch.float16)
+
+
+# ---------------------------------------------------------------------------------------------
+# fused epilogues (no reference counterpart: the reference runs the activation and the residual
+# add as separate vLLM ops; its own analysis of fusing them: docs/EFFICIENCY_INVESTIGATION.md:36-66)
+# ---------------------------------------------------------------------------------------------
+def silu_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """SiluAndMul of [.., 2n] -> [.., n]: fp16(fp16(silu(gate)) * up) (exl3b_silu_mul)."""
+    n = x.shape[-1] // 2
+    x2 = x.reshape(-1, 2 * n)
+    assert x2.dtype == torch.float16 and x2.stride(-1) == 1
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), dtype=torch.float16, device=x.device)
+    o2 = out.view(-1, n)
+    _lib.call("exl3b_silu_mul", x2.data_ptr(), x2.stride(0), o2.data_ptr(), o2.stride(0), x2.shape[0], n,
+              _stream(x.device))
+    return out
+
+
+@torch.library.custom_op("exl3rocm::gate_up_silu", mutates_args=())
+def exl3_gate_up_silu(x: torch.Tensor, trellis: list[torch.Tensor], suh: list[torch.Tensor],
+                      svh: list[torch.Tensor], K: int, mcg: bool, mul1: bool) -> torch.Tensor:
+    """silu(x @ gate) * (x @ up) for the two EXL3 groups of a SwiGLU MLP, [.., n] fp16.  M <= 16: one
+    launch, the activation in the GEMV epilogue; otherwise the grouped route and exl3b_silu_mul."""
+    k = x.shape[-1]
+    n = int(svh[0].shape[0])
+    assert len(trellis) == 2 and int(svh[1].shape[0]) == n
+    x2 = _prep_x(x, k, keep_bf16=(x.numel() // max(k, 1)) <= GEMV_MAX_ROWS)
+    M = x2.shape[0]
+    y = torch.empty((M, n), dtype=torch.float16, device=x.device)
+    if M == 0:
+        return y.view(*x.shape[:-1], n)
+    if M <= GEMV_MAX_ROWS:
+        linear_into(x2, trellis, suh, svh, K, mcg, mul1, y, ACT_SILU_MUL)
+    else:
+        gu = exl3_linear_groups(x2, trellis, suh, svh, [K, K], mcg, mul1)
+        silu_mul(gu, y)
+    return y.view(*x.shape[:-1], n)
+
+
+@exl3_gate_up_silu.register_fake
+def _(x, trellis, suh, svh, K, mcg, mul1):
+    return x.new_empty((*x.shape[:-1], svh[0].shape[0]), dtype=torch.float16)
+
+
+@torch.library.custom_op("exl3rocm::linear_add_", mutates_args=("residual",))
+def exl3_linear_add_(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+                     mcg: bool, mul1: bool, residual: torch.Tensor) -> None:
+    """residual = fp16(residual + x @ W) in place (fp16 [.., n] rows of unit stride).  M <= 16: the
+    add runs in the GEMV epilogue; otherwise the linear, then one fp16 add."""
+    k = x.shape[-1]
+    n = int(svh.shape[0])
+    x2 = _prep_x(x, k, keep_bf16=(x.numel() // max(k, 1)) <= GEMV_MAX_ROWS)
+    M = x2.shape[0]
+    r2 = residual.view(-1, n)
+    assert residual.dtype == torch.float16 and r2.shape[0] == M and r2.stride(-1) == 1
+    if M == 0:
+        return
+    if M <= GEMV_MAX_ROWS:
+        linear_into(x2, [trellis], [suh], [svh], K, mcg, mul1, r2, Y_ADD)
+    else:
+        r2.add_(exl3_linear(x2, trellis, suh, svh, K, mcg, mul1))

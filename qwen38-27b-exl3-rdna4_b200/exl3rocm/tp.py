@@ -20,7 +20,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .ops import GEMV_MAX_ROWS, X_BF16, _cb, _prep_x, _stream, reserve_workspace
+from .ops import GEMV_MAX_ROWS, X_BF16, Y_ADD, _cb, _prep_x, _stream, reserve_workspace
 
 
 class TpComm:
@@ -62,17 +62,23 @@ class TpComm:
 
 
 def linear_tp(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int, mcg: bool,
-              mul1: bool, comm: TpComm) -> torch.Tensor:
-    """Full output of a row-parallel EXL3 linear from this rank's input slice x [..., k/tp]."""
+              mul1: bool, comm: TpComm, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Full output of a row-parallel EXL3 linear from this rank's input slice x [..., k/tp].  With
+    `residual` ([M, n] fp16, unit column stride) the summed result is added into it in place (every
+    rank holds the same residual and adds the same sum) and returned."""
     k = x.shape[-1]
     n = svh.shape[0]
     x2 = _prep_x(x, k, keep_bf16=True)
     M = x2.shape[0]
     if not 1 <= M <= GEMV_MAX_ROWS:
         raise ValueError(f"exl3rocm: linear_tp takes 1..{GEMV_MAX_ROWS} rows, got {M}")
-    y = torch.empty((M, n), dtype=torch.float16, device=x.device)
+    if residual is not None:
+        y = residual.view(-1, n)
+        assert y.dtype == torch.float16 and y.shape[0] == M and y.stride(-1) == 1
+    else:
+        y = torch.empty((M, n), dtype=torch.float16, device=x.device)
     ws = reserve_workspace(x.device, k, n, 1, max(M, 1))
-    cb = _cb(mcg, mul1) | (X_BF16 if x2.dtype == torch.bfloat16 else 0)
+    cb = _cb(mcg, mul1) | (X_BF16 if x2.dtype == torch.bfloat16 else 0) | (Y_ADD if residual is not None else 0)
     _lib.call("exl3b_linear_tp", x2.data_ptr(), M, k, trellis.data_ptr(), n, K, cb, suh.data_ptr(),
               svh.data_ptr(), y.data_ptr(), y.stride(0), ws.data_ptr(), ws.numel(), ctypes.byref(comm.comm),
               _stream(x.device))
