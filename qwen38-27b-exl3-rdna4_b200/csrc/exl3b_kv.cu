@@ -31,7 +31,7 @@ constexpr int kTail = 128;      // exact rows at the end of a sequence (kv_int4.
 constexpr int kExactRows = kSinks + kTail;
 constexpr float kClipStep = 0.075f;  // kv_int4.py:213
 constexpr int kClipSteps = 3;
-constexpr int kMaxSplits = 64;  // kv_int4.py:43
+constexpr int kMaxSplits = 256;  // the reference segments at most 64 ways (kv_int4.py:43); B200 fills with more
 // one split's partial for one (token, query head): acc[128], m, l, padded to 132 floats so that
 // every record starts on a 16-byte boundary (the kernels move it as float4)
 constexpr int kPartialStride = kHD + 4;
@@ -369,9 +369,11 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     int win_base = -1;  // first block index held in bt_win
 
     // ---- Q^T fragments, resident: B[k-slot][n] = Q[row rbase + 8nt + n][dmap], lane (n = g, slots q) ----
-    // The MMAs take the cache values with a bias (int8: 1152 + k, int4: 1024 + nibble), one
-    // instruction cheaper to build than the true values: S^T then carries bias * (sum of the row's q),
-    // removed per score, and O^T carries sum_t P'_t * bias_t, removed at the end (psum).
+    // The K side of the MMAs takes the cache values with a bias (int8: 1152 + k, int4: 1024 + nibble),
+    // one instruction cheaper to build than the true values: S^T then carries bias * (sum of the row's
+    // q), removed per score (a score sums only 128 products).  The V side takes the true values: its
+    // accumulator runs over the whole split, and a bias there would make it carry ~1000 x the signal
+    // and lose the signal's low bits to the accumulation rounding as the split grows.
     uint32_t qb[NT][8][2];
     float qsum[NT][2];  // sum of the fp16 q of rows 2q and 2q+1 of each n-tile
 #pragma unroll
@@ -439,8 +441,8 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     };
 
     const float sl2 = a.score_scale * 1.4426950408889634f;  // scores in the log2 domain
-    // l_i and psum hold this lane's share (its tokens); they are summed over the lane group at the end
-    float m_i[NT][2], l_i[NT][2], lim[NT][2], psum[NT][2];
+    // l_i holds this lane's share (its tokens); it is summed over the lane group at the end
+    float m_i[NT][2], l_i[NT][2], lim[NT][2];
     float acc[NT][8][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -448,7 +450,6 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         for (int h = 0; h < 2; ++h) {
             m_i[nt][h] = -INFINITY;
             l_i[nt][h] = 0.f;
-            psum[nt][h] = 0.f;
             // causal limit of row 2q + h: key t allowed if t <= L - qlen + query index
             const int r = rbase + 8 * nt + 2 * q + h;
             lim[nt][h] = (r < rows) ? (float)(L - qlen + r / G) : -1.f;
@@ -491,7 +492,7 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         // this tile holds exact rows only if it meets the first kSinks or the last kTail positions
         const bool ex_tile = has_exact && (t0 < kSinks || t0 + 31 >= L - kTail);
 
-        // tiles without exact rows run on biased values (see qsum); the others on true values
+        // K of tiles without exact rows runs on biased values (see qsum); the others on true values
         const bool biased = !ex_tile;
         // K fragments of token r of the tile: k-slot pairs (2q, 2q+1) -> kf[c][0], (2q+8, 2q+9) -> kf[c][1];
         // returns the token's k scale, and its bias in kb
@@ -619,7 +620,6 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 l_i[nt][h] = l_i[nt][h] * corr[nt][h] + rsum[nt][h];
-                psum[nt][h] *= corr[nt][h];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     acc[nt][j][h] *= corr[nt][h];
@@ -645,18 +645,6 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
                     }
                 }
             }
-            // bias of the V values the MMA will see for tokens rA, rB (0 on the exact-row path)
-            float wA = 0.f, wB = 0.f;
-            if (biased) {
-                const int rA = 16 * kc + g, rB = rA + 8;
-                if (KV == 8) {
-                    wA = (t0 + rA < t_hi) ? 1152.f : 0.f;
-                    wB = (t0 + rB < t_hi) ? 1152.f : 0.f;
-                } else {
-                    wA = (t0 + rA < t_hi) ? 1024.f + (float)(__float_as_uint(vsc_s[rA]) & 0xFu) : 0.f;
-                    wB = (t0 + rB < t_hi) ? 1024.f + (float)(__float_as_uint(vsc_s[rB]) & 0xFu) : 0.f;
-                }
-            }
             uint32_t pb[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
@@ -664,9 +652,6 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
                 const __half2 hi = __floats2half2_rn(s[nt][kc][2] * vsB, s[nt][kc][3] * vsB);
                 pb[nt][0] = movm_t(h2_as_u32(lo));
                 pb[nt][1] = movm_t(h2_as_u32(hi));
-                // the exact fp16 P' the MMA multiplies, weighted by each token's bias
-                psum[nt][0] = fmaf(__low2float(hi), wB, fmaf(__low2float(lo), wA, psum[nt][0]));
-                psum[nt][1] = fmaf(__high2float(hi), wB, fmaf(__high2float(lo), wA, psum[nt][1]));
             }
             // V^T A fragments: tokens T0..T3 = 16kc + (2q, 2q+1, 2q+8, 2q+9); m-tile j rows g / g+8 are
             // d = 16g + 2j / 16g + 2j + 1.  va[j][0..3] = (a0, a1, a2, a3)
@@ -684,38 +669,44 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
                         w[T][0] = v4.x ^ 0x80808080u; w[T][1] = v4.y ^ 0x80808080u;
                         w[T][2] = v4.z ^ 0x80808080u; w[T][3] = v4.w ^ 0x80808080u;
                     }
+                    const __half2 bias = u32_as_h2(0x64806480u);  // 1152
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {  // 1152 + v, exact in fp16
+                    for (int j = 0; j < 8; ++j) {  // (1152 + v) - 1152 = v, exact in fp16
                         const uint32_t sel = (j & 1) ? 0x7362u : 0x5140u;
 #pragma unroll
                         for (int pr = 0; pr < 2; ++pr) {  // token pairs (T0, T1) and (T2, T3)
                             const uint32_t x = prmt(w[2 * pr][j >> 1], w[2 * pr + 1][j >> 1], sel);
-                            va[j][2 * pr] = prmt(x, 0x64646464u, 0x5140u);
-                            va[j][2 * pr + 1] = prmt(x, 0x64646464u, 0x7362u);
+                            va[j][2 * pr] = h2_as_u32(__hsub2(u32_as_h2(prmt(x, 0x64646464u, 0x5140u)), bias));
+                            va[j][2 * pr + 1] = h2_as_u32(__hsub2(u32_as_h2(prmt(x, 0x64646464u, 0x7362u)), bias));
                         }
                     }
                 } else {
-                    uint32_t w[4][2];
+                    uint32_t w[4][2], zp[4];
 #pragma unroll
                     for (int T = 0; T < 4; ++T) {
                         uint4 v4 = make_uint4(0u, 0u, 0u, 0u);
                         if (t0 + rT[T] < t_hi) v4 = chunk_at(1, rT[T], g >> 1);
                         w[T][0] = (g & 1) ? v4.z : v4.x;
                         w[T][1] = (g & 1) ? v4.w : v4.y;
+                        zp[T] = 0x6400u | (__float_as_uint(vsc_s[rT[T]]) & 0xFu);  // 1024 + zero point
                     }
+                    // (1024 + nibble) - (1024 + zp) = nibble - zp, exact in fp16; a register holds
+                    // tokens (T0, T1) or (T2, T3)
+                    const __half2 zq[2] = {u32_as_h2(zp[0] | (zp[1] << 16)), u32_as_h2(zp[2] | (zp[3] << 16))};
 #pragma unroll
                     for (int i = 0; i < 2; ++i)
 #pragma unroll
                         for (int kk = 0; kk < 4; kk += 2) {  // bytes (kk, kk+1) of word i -> m-tiles 4i+kk, 4i+kk+1
                             const uint32_t sel = kk ? 0x7362u : 0x5140u;
 #pragma unroll
-                            for (int pr = 0; pr < 2; ++pr) {  // 1024 + nibble
+                            for (int pr = 0; pr < 2; ++pr) {
                                 const uint32_t x = prmt(w[2 * pr][i], w[2 * pr + 1][i], sel);
                                 const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
-                                va[4 * i + kk][2 * pr] = prmt(lo, 0x64646464u, 0x5140u);
-                                va[4 * i + kk][2 * pr + 1] = prmt(hi, 0x64646464u, 0x5140u);
-                                va[4 * i + kk + 1][2 * pr] = prmt(lo, 0x64646464u, 0x7362u);
-                                va[4 * i + kk + 1][2 * pr + 1] = prmt(hi, 0x64646464u, 0x7362u);
+                                auto nz = [&](uint32_t u) { return h2_as_u32(__hsub2(u32_as_h2(u), zq[pr])); };
+                                va[4 * i + kk][2 * pr] = nz(prmt(lo, 0x64646464u, 0x5140u));
+                                va[4 * i + kk][2 * pr + 1] = nz(prmt(hi, 0x64646464u, 0x5140u));
+                                va[4 * i + kk + 1][2 * pr] = nz(prmt(lo, 0x64646464u, 0x7362u));
+                                va[4 * i + kk + 1][2 * pr + 1] = nz(prmt(hi, 0x64646464u, 0x7362u));
                             }
                         }
                 }
@@ -767,23 +758,15 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     }
     cp_async_wait<0>();
 
-    // lane shares of l and of the bias sums -> row totals (the lanes of a row differ in g)
+    // lane shares of l -> row totals (the lanes of a row differ in g)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            float l = l_i[nt][h], ps = psum[nt][h];
+            float l = l_i[nt][h];
 #pragma unroll
-            for (int d = 4; d <= 16; d <<= 1) {
-                l += __shfl_xor_sync(0xFFFFFFFFu, l, d);
-                ps += __shfl_xor_sync(0xFFFFFFFFu, ps, d);
-            }
+            for (int d = 4; d <= 16; d <<= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, d);
             l_i[nt][h] = l;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                acc[nt][j][h] -= ps;
-                acc[nt][j][2 + h] -= ps;
-            }
         }
 
     // ---- partial of this split: acc (d order restored), m, l ----
@@ -822,43 +805,79 @@ struct KvReduceArgs {
     const float* unrot_signs;  // int4: RHT signs, else null
 };
 
-__global__ void kv_reduce_kernel(const KvReduceArgs a) {
-    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (item >= (int64_t)a.num_tokens * a.num_q_heads) return;
-    const int lane = threadIdx.x & 31;
+// One CTA per (query token, q head).  The split maxima and row sums are read by one thread per
+// split and reduced over the CTA; warp j then accumulates splits j, j + 8, ... of the weighted
+// outputs and warp 0 sums the eight partial vectors in warp order (a fixed order: deterministic).
+constexpr int kReduceThreads = 256;
+constexpr int kReduceWarps = kReduceThreads / 32;
+static_assert(kMaxSplits <= kReduceThreads, "one thread per split");
+
+__global__ void __launch_bounds__(kReduceThreads) kv_reduce_kernel(const KvReduceArgs a) {
+    const int64_t item = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = (int)(item / a.num_q_heads);
     const int s = seq_of_token(a.query_start_loc, a.num_seqs, t);
     const int L = a.seq_lens[s];
     const int per = ((L + a.num_splits - 1) / a.num_splits + 31) & ~31;
     const int nsp = (L + per - 1) / per;  // splits that held tokens
     const float* base = a.partial + item * a.num_splits * kPartialStride;
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsp; ++sp) M = fmaxf(M, base[sp * kPartialStride + kHD]);
-    float v[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
-    if (M != -INFINITY) {
-        for (int sp = 0; sp < nsp; ++sp) {
-            const float* p = base + sp * kPartialStride;
-            const float ms = p[kHD];
-            if (ms == -INFINITY) continue;
-            const float w = exp_f(ms - M);
-            lsum += w * p[kHD + 1];
-            const float4 x = reinterpret_cast<const float4*>(p)[lane];
-            v[0] += w * x.x; v[1] += w * x.y; v[2] += w * x.z; v[3] += w * x.w;
-        }
+    __shared__ float w_s[kMaxSplits];
+    __shared__ float red_m[kReduceWarps], red_l[kReduceWarps];
+    __shared__ float4 acc_s[kReduceWarps][32];
+    const int sp = threadIdx.x;
+    float ms = -INFINITY, ls = 0.f;
+    if (sp < nsp) {
+        ms = base[sp * kPartialStride + kHD];
+        ls = base[sp * kPartialStride + kHD + 1];
+    }
+    float M = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    if (lane == 0) red_m[warp] = M;
+    __syncthreads();
+    M = red_m[0];
+#pragma unroll
+    for (int i = 1; i < kReduceWarps; ++i) M = fmaxf(M, red_m[i]);
+    const float w = (ms == -INFINITY) ? 0.f : exp_f(ms - M);  // M is finite when any split is
+    float l = w * ls;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+    if (lane == 0) red_l[warp] = l;
+    if (sp < kMaxSplits) w_s[sp] = w;
+    __syncthreads();
+    float lsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kReduceWarps; ++i) lsum += red_l[i];
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int j = warp; j < nsp; j += kReduceWarps) {
+        const float wj = w_s[j];
+        if (wj == 0.f) continue;
+        const float4 x = reinterpret_cast<const float4*>(base + j * kPartialStride)[lane];
+        v.x += wj * x.x; v.y += wj * x.y; v.z += wj * x.z; v.w += wj * x.w;
+    }
+    acc_s[warp][lane] = v;
+    __syncthreads();
+    if (warp != 0) return;
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < kReduceWarps; ++i) {
+        const float4 x = acc_s[i][lane];
+        r[0] += x.x; r[1] += x.y; r[2] += x.z; r[3] += x.w;
     }
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] *= inv;
+    for (int i = 0; i < 4; ++i) r[i] *= inv;
     if (a.unrot_signs) {
         // the reference stores the rotated output as fp16 before un-rotating (kv_int4.py:539-563)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = __half2float(__float2half_rn(v[i]));
-        had128_warp(v);
+        for (int i = 0; i < 4; ++i) r[i] = __half2float(__float2half_rn(r[i]));
+        had128_warp(r);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = v[i] * a.unrot_signs[4 * lane + i] * (1.f / kHD);
+        for (int i = 0; i < 4; ++i) r[i] = r[i] * a.unrot_signs[4 * lane + i] * (1.f / kHD);
     }
     reinterpret_cast<uint2*>(a.out + item * kHD)[lane] =
-        make_uint2(h2_as_u32(__floats2half2_rn(v[0], v[1])), h2_as_u32(__floats2half2_rn(v[2], v[3])));
+        make_uint2(h2_as_u32(__floats2half2_rn(r[0], r[1])), h2_as_u32(__floats2half2_rn(r[2], r[3])));
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -933,11 +952,15 @@ static int kv_num_sms() {
     return v > 0 ? v : 148;
 }
 
-static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len) {
-    // twelve single-warp CTAs per SM fit (registers and shared memory): fill them in one wave
-    // (rounded down: a few CTAs more than the slots would run as a second, almost empty wave)
+// Splits of the key range per (sequence, KV head).  Twelve single-warp CTAs per SM fit (registers
+// and shared memory): fill them in one wave (rounded down: a few CTAs more than the slots would
+// run as a second, almost empty wave).  A split must stream enough keys to pay for its start-up:
+// 128 for up to 8 query rows per KV head (decode), 256 above (speculative verify).  rows = 1
+// gives the most splits any call of the shape can take (the workspace bound).
+static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len, int rows) {
     const int want = (12 * kv_num_sms()) / (num_seqs * num_kv_heads);
-    const int by_len = (max_seq_len + 63) / 64;
+    const int min_keys = rows <= 8 ? 128 : 256;
+    const int by_len = (max_seq_len + min_keys - 1) / min_keys;
     return std::max(1, std::min(kMaxSplits, std::min(want, by_len)));
 }
 
@@ -1026,7 +1049,7 @@ extern "C" int exl3b_kv_int4_write(const void* key, const void* value, int dtype
 extern "C" size_t exl3b_kv_attn_workspace_bytes(int num_tokens, int num_q_heads, int num_seqs, int num_kv_heads,
                                                 int max_seq_len) {
     if (num_tokens <= 0 || num_q_heads <= 0 || num_seqs <= 0 || num_kv_heads <= 0) return 0;
-    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len));
+    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len), 1);
     const size_t qr = (size_t)num_tokens * num_q_heads * kHD * 2;
     return (qr + 255) / 256 * 256 + (size_t)num_tokens * num_q_heads * S * kPartialStride * 4;
 }
@@ -1050,7 +1073,7 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     if (ws_bytes < exl3b_kv_attn_workspace_bytes(num_tokens, num_q_heads, num_seqs, num_kv_heads, max_seq_len))
         return EXL3B_WORKSPACE;
     cudaStream_t st = (cudaStream_t)stream;
-    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len));
+    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len), max_q_len * G);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const size_t qr_bytes = ((size_t)num_tokens * num_q_heads * kHD * 2 + 255) / 256 * 256;
     const __half* qin = reinterpret_cast<const __half*>(q);
@@ -1087,7 +1110,7 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     r.query_start_loc = query_start_loc; r.num_seqs = num_seqs; r.num_tokens = num_tokens;
     r.num_q_heads = num_q_heads; r.num_splits = S; r.unrot_signs = kv == 4 ? rht_signs : nullptr;
     const int64_t items = (int64_t)num_tokens * num_q_heads;
-    kv_reduce_kernel<<<(unsigned)((items + 7) / 8), 256, 0, st>>>(r);
+    kv_reduce_kernel<<<(unsigned)items, kReduceThreads, 0, st>>>(r);
     return cuda_status(cudaGetLastError());
 }
 

@@ -206,3 +206,47 @@ class SyntheticDecoder:
         """This library's kernel launches in one step: per layer rmsnorm x2, 4 linears, rope, the KV
         write, the attention and its split combine; then the final norm and the lm_head."""
         return self.s.layers * 10 + 2
+
+
+def main(argv=None) -> None:
+    """python -m exl3rocm.synthetic [--batch B] [--q-len Q] [--ctx N] [--layers L] [--steps S]
+    Times CUDA-graph replays of the decode step and prints one JSON line."""
+    import argparse
+    import json
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--q-len", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--layers", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dec = SyntheticDecoder(DecoderShape(layers=a.layers), dev, batch=a.batch, q_len=a.q_len, ctx=a.ctx, seed=2024)
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    dec.reserve(st)
+    tokens = torch.randint(0, dec.s.vocab, (dec.M,), device=dev)
+    with torch.cuda.stream(st):
+        dec.step(tokens)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            dec.step(tokens)
+            tokens.copy_(dec.next_tokens)
+        for _ in range(a.warmup):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(a.steps):
+            graph.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    print(json.dumps({"batch": a.batch, "q_len": a.q_len, "ctx": a.ctx, "layers": a.layers, "ms_per_step": ms,
+                      "rows_per_s": dec.M / (ms * 1e-3), "weight_bytes": dec.weight_bytes(),
+                      "kv_bytes": dec.kv_bytes()}))
+    del graph
+
+
+if __name__ == "__main__":
+    main()

@@ -110,6 +110,9 @@ def _int8_setup(rng, seq_lens, q_lens):
 @pytest.mark.parametrize("seq_lens,q_lens", [
     ([1], [1]), ([33], [1]), ([1000], [1]), ([5, 300, 64, 4096], [1, 1, 1, 1]),
     ([40, 700], [4, 4]), ([17], [3]), ([2500], [2]),
+    # a batch-8 decode at long context: ~27 splits of ~600 keys per (sequence, KV head), so one
+    # split's accumulator runs over hundreds of tokens
+    ([16384] * 8, [1] * 8),
 ])
 def test_int8_attention(kv, seq_lens, q_lens):
     rng = np.random.default_rng(sum(seq_lens) + 7 * sum(q_lens))
@@ -229,7 +232,17 @@ def test_int4_write_with_exact_rows_bitexact(kv):
                                              ([700, 20], [4, 4]), ([3000], [1])])
 def test_int4_attention_with_exact_rows(kv, seq_lens, q_lens):
     rng = np.random.default_rng(sum(seq_lens) + 3)
-    slots = [3, 1, 0][: len(seq_lens)]
+    _check_int4_attention(kv, rng, seq_lens, q_lens, [3, 1, 0][: len(seq_lens)])
+
+
+def test_int4_attention_long_splits(kv):
+    """Eight sequences of 8192 without exact rows: every tile on the packed path, ~27 splits of ~300
+    keys per (sequence, KV head)."""
+    rng = np.random.default_rng(8192)
+    _check_int4_attention(kv, rng, [8192] * 8, [1] * 8, [-1] * 8)
+
+
+def _check_int4_attention(kv, rng, seq_lens, q_lens, slots):
     bt, dev, ora = _int4_world(kv, rng, seq_lens, q_lens, slots)
     kc, vc, ks, vs = dev
     ko, vo, kso, vso, exk, exv, tag = ora
