@@ -316,18 +316,20 @@ def bench_prefill(torch, dev, K: int, m: int = 2048, iters: int = 5) -> dict:
 
 
 def bench_decode(torch, dev, steps: int, warmup: int, ctx: int = 32768,
-                 cases=((1, 1), (8, 1), (1, 4))) -> list:
+                 cases=((1, 1), (8, 1), (1, 4)), world: int = 1, rank: int = 0, comm=None, pg=None) -> list:
     """Decode tokens/s of the synthetic 64-layer 27B-class decoder (exl3rocm.synthetic) with an int8
     paged KV cache of ctx tokens per sequence: (batch, q_len) = (1, 1) and (8, 1) decode, (1, 4) a
     4-token speculative verify.  Each step is one CUDA-graph replay of embed -> 64 layers -> lm_head
     -> argmax, fed the previous step's tokens on the device; timed with CUDA events over `steps`
     replays after `warmup`.  e2e adds, every step, the input tokens from pinned host memory and the
-    output tokens back to it.  Weights (9.5 GB) and caches exceed L2 many times over."""
+    output tokens back to it.  Weights (9.5 GB) and caches exceed L2 many times over.
+    world > 1: tensor parallel over the ranks (exl3rocm.synthetic), times as the max over ranks."""
     from exl3rocm.synthetic import DecoderShape, SyntheticDecoder
     shape = DecoderShape()
     out, base = [], None
     for batch, q_len in cases:
-        dec = SyntheticDecoder(shape, dev, batch=batch, q_len=q_len, ctx=ctx, seed=2024, weights_of=base)
+        dec = SyntheticDecoder(shape, dev, batch=batch, q_len=q_len, ctx=ctx, seed=2024, weights_of=base,
+                               tp_size=world, tp_rank=rank, comm=comm, group=pg)
         base = base or dec
         st = torch.cuda.Stream(dev)
         st.wait_stream(torch.cuda.current_stream(dev))
@@ -362,13 +364,17 @@ def bench_decode(torch, dev, steps: int, warmup: int, ctx: int = 32768,
             e1.record(st)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms, e2e_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=pg)
+            ms, e2e_ms = float(t[0]), float(t[1])
         wb, kb = dec.weight_bytes(), dec.kv_bytes()
         out.append({"batch": batch, "q_len": q_len, "ctx": ctx, "ms_per_step": ms,
                     "tok_s": batch / (ms * 1e-3) if q_len == 1 else None,
                     "rows_per_s": dec.M / (ms * 1e-3), "e2e_ms_per_step": e2e_ms,
                     "e2e_tok_s": batch / (e2e_ms * 1e-3) if q_len == 1 else None,
                     "weight_bytes": wb, "kv_bytes": kb, "gb_s": (wb + kb) / (ms * 1e-3) / 1e9,
-                    "gpu_launches_per_step": dec.launches_per_step()})
+                    "gpu_launches_per_step": dec.launches_per_step(), "tp": world})
         del graph
         if dec is not base:
             del dec
@@ -574,10 +580,12 @@ def main():
                                  for kind, ctx, b, ql in ((8, 32768, 8, 1), (4, 32768, 8, 1), (8, 32768, 1, 4),
                                                           (4, 65536, 1, 1), (8, 4096, 8, 1))]
         extra["prefill_m2048"] = bench_prefill(torch, dev, K)
-        if not args.no_decode:
-            del layers, outs, inputs
-            torch.cuda.empty_cache()
-            extra["decode"] = bench_decode(torch, dev, steps=max(10, args.steps), warmup=args.warmup)
+
+    if not args.no_extra and not args.no_decode and (world == 1 or comm is not None):
+        del layers, outs, inputs
+        torch.cuda.empty_cache()
+        extra["decode"] = bench_decode(torch, dev, steps=max(10, args.steps), warmup=args.warmup, world=world,
+                                       rank=rank, comm=comm, pg=pg)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

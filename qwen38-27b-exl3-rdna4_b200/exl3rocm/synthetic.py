@@ -1,4 +1,5 @@
-"""A synthetic dense decoder for measuring decode tokens/s through this library alone.
+"""A synthetic dense decoder for measuring decode tokens/s through this library alone, on one GPU
+or tensor-parallel over several.
 
 The workload is the 27B-class decoder shape the decode tok/s metric is quoted on: 64 layers,
 hidden 5120, 40 q / 8 kv heads of 128, SwiGLU 17408, vocab 151936, RMSNorm, neox RoPE
@@ -14,6 +15,13 @@ One step (``step``) runs, for M = batch * q_len query rows:
   -> paged int8 attention -> o (+ residual in the epilogue) -> rmsnorm -> gate/up with SiLU * up
   in the epilogue -> down (+ residual in the epilogue) ] -> rmsnorm -> lm_head -> argmax
 All buffers are allocated up front, so the step can be captured in a CUDA graph.
+
+Tensor parallel (tp_size > 1, one process per GPU): every rank draws the whole model from the same
+seed, layer by layer, and keeps its shard, so the sharded model is the single-GPU model.  q/k/v
+are split by heads and gate/up by columns (no exchange); o and down by their inputs, summed across
+ranks inside the GEMV through peer memory (exl3b_linear_tp) with the residual add in the same
+epilogue; each rank caches its own KV heads; the lm_head is split in whole 128-column blocks, and
+the ranks' (max, index) pairs are all-gathered (NCCL) to pick the next tokens.
 """
 from __future__ import annotations
 
@@ -46,12 +54,8 @@ class DecoderShape:
     bits_head: int = 4
     block_size: int = 16
 
-    def weights_per_layer(self) -> int:
-        qkv = self.hidden * (self.q_heads + 2 * self.kv_heads) * self.head
-        return qkv + self.q_heads * self.head * self.hidden + 3 * self.hidden * self.intermediate
-
     def layer_bytes(self) -> int:
-        """Trellis bytes one layer streams per step."""
+        """Trellis bytes one layer streams per step (all ranks together)."""
         h, d = self.hidden, self.head
         qkv = h * (self.q_heads + 2 * self.kv_heads) * d * self.bits_qkv
         o = self.q_heads * d * h * self.bits_o
@@ -63,67 +67,123 @@ class DecoderShape:
 class Exl3Weight:
     """One EXL3 matrix k -> n: trellis int16 [k/16][n/16][16K], suh fp16 [k], svh fp16 [n]."""
 
-    def __init__(self, gen: torch.Generator, k: int, n: int, K: int, device):
+    def __init__(self, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int):
+        self.trellis, self.suh, self.svh, self.K = trellis, suh, svh, K
+        self.k, self.n = suh.shape[0], svh.shape[0]
+
+    @staticmethod
+    def random(gen: torch.Generator, k: int, n: int, K: int, device) -> "Exl3Weight":
         codes = torch.randint(0, 65536, (k // 16, n // 16, 16 * K), generator=gen, device=device, dtype=torch.int32)
-        self.trellis = codes.to(torch.int16)
+        trellis = codes.to(torch.int16)
         del codes
-        self.suh = (torch.randint(0, 2, (k,), generator=gen, device=device) * 2 - 1).to(torch.float16)
-        self.svh = ((torch.randint(0, 2, (n,), generator=gen, device=device) * 2 - 1) / math.sqrt(k)).to(torch.float16)
-        self.k, self.n, self.K = k, n, K
+        suh = (torch.randint(0, 2, (k,), generator=gen, device=device) * 2 - 1).to(torch.float16)
+        svh = ((torch.randint(0, 2, (n,), generator=gen, device=device) * 2 - 1) / math.sqrt(k)).to(torch.float16)
+        return Exl3Weight(trellis, suh, svh, K)
+
+    def columns(self, n0: int, n1: int) -> "Exl3Weight":
+        """Output columns [n0, n1) (multiples of 128): a column-parallel shard."""
+        return Exl3Weight(self.trellis[:, n0 // 16:n1 // 16].contiguous(), self.suh, self.svh[n0:n1].contiguous(),
+                          self.K)
+
+    def rows(self, k0: int, k1: int) -> "Exl3Weight":
+        """Input features [k0, k1) (multiples of 128): a row-parallel shard."""
+        return Exl3Weight(self.trellis[k0 // 16:k1 // 16].contiguous(), self.suh[k0:k1].contiguous(), self.svh,
+                          self.K)
 
 
 class Layer:
-    def __init__(self, gen, s: DecoderShape, device):
+    """One layer's weights, drawn whole (the same draw at every tensor-parallel size) and sharded."""
+
+    def __init__(self, gen, s: DecoderShape, device, tp: int = 1, rank: int = 0):
         h, d = s.hidden, s.head
-        self.q = Exl3Weight(gen, h, s.q_heads * d, s.bits_qkv, device)
-        self.k = Exl3Weight(gen, h, s.kv_heads * d, s.bits_qkv, device)
-        self.v = Exl3Weight(gen, h, s.kv_heads * d, s.bits_qkv, device)
-        self.o = Exl3Weight(gen, s.q_heads * d, h, s.bits_o, device)
-        self.gate = Exl3Weight(gen, h, s.intermediate, s.bits_gate_up, device)
-        self.up = Exl3Weight(gen, h, s.intermediate, s.bits_gate_up, device)
-        self.down = Exl3Weight(gen, s.intermediate, h, s.bits_down, device)
+        qd, kd, it = s.q_heads * d // tp, s.kv_heads * d // tp, s.intermediate // tp
+        q = Exl3Weight.random(gen, h, s.q_heads * d, s.bits_qkv, device)
+        k = Exl3Weight.random(gen, h, s.kv_heads * d, s.bits_qkv, device)
+        v = Exl3Weight.random(gen, h, s.kv_heads * d, s.bits_qkv, device)
+        o = Exl3Weight.random(gen, s.q_heads * d, h, s.bits_o, device)
+        gate = Exl3Weight.random(gen, h, s.intermediate, s.bits_gate_up, device)
+        up = Exl3Weight.random(gen, h, s.intermediate, s.bits_gate_up, device)
+        down = Exl3Weight.random(gen, s.intermediate, h, s.bits_down, device)
+        if tp == 1:
+            self.q, self.k, self.v, self.o, self.gate, self.up, self.down = q, k, v, o, gate, up, down
+        else:
+            self.q, self.k, self.v = (q.columns(rank * qd, (rank + 1) * qd), k.columns(rank * kd, (rank + 1) * kd),
+                                      v.columns(rank * kd, (rank + 1) * kd))
+            self.o = o.rows(rank * qd, (rank + 1) * qd)
+            self.gate, self.up = gate.columns(rank * it, (rank + 1) * it), up.columns(rank * it, (rank + 1) * it)
+            self.down = down.rows(rank * it, (rank + 1) * it)
         self.norm_in = (1.0 + 0.1 * torch.randn(h, generator=gen, device=device)).to(torch.float16)
         self.norm_post = (1.0 + 0.1 * torch.randn(h, generator=gen, device=device)).to(torch.float16)
 
 
+def head_columns(vocab: int, tp: int, rank: int) -> tuple:
+    """This rank's lm_head columns: whole 128-column blocks, ceil(blocks / tp) per rank."""
+    blocks = vocab // 128
+    per = -(-blocks // tp)
+    b0, b1 = min(blocks, rank * per), min(blocks, (rank + 1) * per)
+    return b0 * 128, b1 * 128
+
+
 class SyntheticDecoder:
     """Weights, an int8 paged KV cache of `ctx` tokens for each of `batch` sequences, and the
-    buffers of one decode step of q_len tokens per sequence (the last q_len positions of ctx)."""
+    buffers of one decode step of q_len tokens per sequence (the last q_len positions of ctx).
+
+    tp_size > 1: this rank's shard; `comm` is an exl3rocm.tp.TpComm over the ranks (o and down
+    reduce through it) and `group` the process group of the next-token all-gather."""
 
     def __init__(self, shape: DecoderShape, device, batch: int = 1, q_len: int = 1, ctx: int = 32768,
-                 seed: int = 0, weights_of: "SyntheticDecoder | None" = None):
-        """weights_of: take the weights of another decoder of the same shape (a different batch,
-        query length or context over the same model)."""
+                 seed: int = 0, weights_of: "SyntheticDecoder | None" = None, tp_size: int = 1, tp_rank: int = 0,
+                 comm=None, group=None):
+        """weights_of: take the weights of another decoder of the same shape and sharding (a different
+        batch, query length or context over the same model)."""
         s = self.s = shape
         self.device = device = torch.device(device)
         self.batch, self.q_len, self.ctx = batch, q_len, ctx
+        self.tp, self.rank, self.comm, self.group = tp_size, tp_rank, comm, group
         M = self.M = batch * q_len
         if M > ops.GEMV_MAX_ROWS:
             raise ValueError(f"decode step of {M} rows: the fused linears take 1..{ops.GEMV_MAX_ROWS}")
         if ctx % s.block_size or q_len > ctx:
             raise ValueError("ctx must be a multiple of the block size and >= q_len")
+        tp = tp_size
+        if tp > 1:
+            if comm is None:
+                raise ValueError("tensor parallel decode needs a TpComm")
+            if s.q_heads % tp or s.kv_heads % tp or (s.intermediate // 128) % tp:
+                raise ValueError(f"heads and intermediate blocks must divide by tp {tp}")
+            if (s.q_heads * s.head // tp) % 128:
+                raise ValueError("row-parallel shards must be whole 128-blocks")
+        self.hq, self.hkv = s.q_heads // tp, s.kv_heads // tp
+        self.v0, self.v1 = head_columns(s.vocab, tp, tp_rank)
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
         if weights_of is not None:
-            assert weights_of.s == s
+            assert weights_of.s == s and weights_of.tp == tp and weights_of.rank == tp_rank
             self.layers, self.embed = weights_of.layers, weights_of.embed
             self.norm_final, self.head = weights_of.norm_final, weights_of.head
         else:
-            self.layers = [Layer(gen, s, device) for _ in range(s.layers)]
+            self.layers = [Layer(gen, s, device, tp, tp_rank) for _ in range(s.layers)]
             self.embed = (torch.randn(s.vocab, s.hidden, generator=gen, device=device)).to(torch.float16)
             self.norm_final = (1.0 + 0.1 * torch.randn(s.hidden, generator=gen, device=device)).to(torch.float16)
-            self.head = Exl3Weight(gen, s.hidden, s.vocab, s.bits_head, device)
-        # int8 paged cache: sequence b owns blocks [b * bps, (b + 1) * bps)
+            head = Exl3Weight.random(gen, s.hidden, s.vocab, s.bits_head, device)
+            self.head = head if tp == 1 else head.columns(self.v0, self.v1)
+            del head
+        # int8 paged cache: sequence b owns blocks [b * bps, (b + 1) * bps); drawn for all heads and
+        # sliced to this rank's, so the cache contents do not depend on the sharding either
         bps = ctx // s.block_size
         nblk = batch * bps
+        h0, h1 = tp_rank * self.hkv, (tp_rank + 1) * self.hkv
         self.k_cache, self.v_cache, self.k_scale, self.v_scale = [], [], [], []
         for _ in range(s.layers):
-            self.k_cache.append(torch.randint(-127, 128, (nblk, s.block_size, s.kv_heads, s.head), generator=gen,
-                                              device=device, dtype=torch.int8))
-            self.v_cache.append(torch.randint(-127, 128, (nblk, s.block_size, s.kv_heads, s.head), generator=gen,
-                                              device=device, dtype=torch.int8))
-            self.k_scale.append(torch.rand((nblk, s.block_size, s.kv_heads), generator=gen, device=device) * 0.02)
-            self.v_scale.append(torch.rand((nblk, s.block_size, s.kv_heads), generator=gen, device=device) * 0.02)
+            for dst, is_rows in ((self.k_cache, True), (self.v_cache, True), (self.k_scale, False),
+                                 (self.v_scale, False)):
+                if is_rows:
+                    full = torch.randint(-127, 128, (nblk, s.block_size, s.kv_heads, s.head), generator=gen,
+                                         device=device, dtype=torch.int8)
+                else:
+                    full = torch.rand((nblk, s.block_size, s.kv_heads), generator=gen, device=device) * 0.02
+                dst.append(full if tp == 1 else full[:, :, h0:h1].contiguous())
+                del full
         self.block_table = torch.arange(nblk, dtype=torch.int32, device=device).view(batch, bps)
         pos = torch.arange(ctx - q_len, ctx, dtype=torch.int64, device=device).repeat(batch)
         self.positions = pos
@@ -134,61 +194,72 @@ class SyntheticDecoder:
         self.cu_q = torch.arange(0, batch + 1, dtype=torch.int32, device=device) * q_len
         self.cos_sin = rope_cos_sin(ctx, s.rope_theta, device, s.head)
         # step buffers
-        qd, kd = s.q_heads * s.head, s.kv_heads * s.head
+        qd, kd = self.hq * s.head, self.hkv * s.head
         self.residual = torch.empty(M, s.hidden, dtype=torch.float16, device=device)
         self.h = torch.empty(M, s.hidden, dtype=torch.float16, device=device)
         self.qkv = torch.empty(M, qd + 2 * kd, dtype=torch.float16, device=device)
         self.q = torch.empty(M, qd, dtype=torch.float16, device=device)
         self.attn = torch.empty(M, qd, dtype=torch.float16, device=device)
-        self.act = torch.empty(M, s.intermediate, dtype=torch.float16, device=device)
-        self.logits = torch.empty(M, s.vocab, dtype=torch.float16, device=device)
+        self.act = torch.empty(M, s.intermediate // tp, dtype=torch.float16, device=device)
+        self.logits = torch.empty(M, self.v1 - self.v0, dtype=torch.float16, device=device)
         self.next_tokens = torch.empty(M, dtype=torch.int64, device=device)
+        if tp > 1:
+            self.pick = torch.empty(M, 2, dtype=torch.float32, device=device)
+            self.picks = torch.empty(tp * M, 2, dtype=torch.float32, device=device)
         self.reserve()
 
     def reserve(self, stream: torch.cuda.Stream | None = None) -> None:
         """Workspaces of every call of the step on `stream` (the current one by default), so that a
         capture on it allocates nothing."""
         s, M, dev = self.s, self.M, self.device
-        qd, kd = s.q_heads * s.head, s.kv_heads * s.head
+        qd, kd, it = self.hq * s.head, self.hkv * s.head, s.intermediate // self.tp
         ctx = torch.cuda.stream(stream) if stream is not None else torch.cuda.stream(torch.cuda.current_stream(dev))
         with ctx:
-            for k, n, g in ((s.hidden, qd + 2 * kd, 3), (qd, s.hidden, 1), (s.hidden, 2 * s.intermediate, 2),
-                            (s.intermediate, s.hidden, 1), (s.hidden, s.vocab, 1)):
+            for k, n, g in ((s.hidden, qd + 2 * kd, 3), (qd, s.hidden, 1), (s.hidden, 2 * it, 2),
+                            (it, s.hidden, 1), (s.hidden, self.v1 - self.v0, 1)):
                 ops.reserve_workspace(dev, k, n, g, M)
-            kv.reserve_attention_workspace(dev, M, s.q_heads, self.batch, s.kv_heads, self.ctx)
+            kv.reserve_attention_workspace(dev, M, self.hq, self.batch, self.hkv, self.ctx)
 
     def weight_bytes(self) -> int:
-        """Trellis bytes streamed per step (all layers and the lm_head)."""
+        """Trellis bytes one step streams, all ranks together (all layers and the lm_head)."""
         return self.s.layers * self.s.layer_bytes() + self.s.hidden * self.s.vocab * self.s.bits_head // 8
 
     def kv_bytes(self) -> int:
-        """KV cache bytes the attention reads per step (int8 rows + fp32 scales, K and V)."""
+        """KV cache bytes the attention reads per step, all ranks together (int8 rows + fp32 scales)."""
         s = self.s
         return s.layers * self.batch * self.ctx * s.kv_heads * (2 * s.head + 8)
 
     def layer_forward(self, i: int) -> None:
         s, L = self.s, self.layers[i]
-        qd, kd, M = s.q_heads * s.head, s.kv_heads * s.head, self.M
+        qd, kd, M = self.hq * s.head, self.hkv * s.head, self.M
         mcg, mul1 = CB
         rmsnorm(self.residual, L.norm_in, s.eps, out=self.h)
         ops.linear_into(self.h, [L.q.trellis, L.k.trellis, L.v.trellis], [L.q.suh, L.k.suh, L.v.suh],
                         [L.q.svh, L.k.svh, L.v.svh], s.bits_qkv, mcg, mul1, self.qkv)
-        rope_neox(self.qkv, self.q, s.q_heads, s.kv_heads, self.positions, self.cos_sin)
-        key = self.qkv[:, qd:qd + kd].view(M, s.kv_heads, s.head)
-        val = self.qkv[:, qd + kd:].view(M, s.kv_heads, s.head)
+        rope_neox(self.qkv, self.q, self.hq, self.hkv, self.positions, self.cos_sin)
+        key = self.qkv[:, qd:qd + kd].view(M, self.hkv, s.head)
+        val = self.qkv[:, qd + kd:].view(M, self.hkv, s.head)
         kv.reshape_and_cache_int8(key, val, self.k_cache[i], self.v_cache[i], self.slot_mapping, self.k_scale[i],
                                   self.v_scale[i])
-        kv.attention_int8(q=self.q.view(M, s.q_heads, s.head), k=self.k_cache[i], v=self.v_cache[i],
-                          out=self.attn.view(M, s.q_heads, s.head), cu_seqlens_q=self.cu_q, max_seqlen_q=self.q_len,
+        kv.attention_int8(q=self.q.view(M, self.hq, s.head), k=self.k_cache[i], v=self.v_cache[i],
+                          out=self.attn.view(M, self.hq, s.head), cu_seqlens_q=self.cu_q, max_seqlen_q=self.q_len,
                           seqused_k=self.seq_lens, block_table=self.block_table,
                           softmax_scale=1.0 / math.sqrt(s.head), k_scale_cache=self.k_scale[i],
                           v_scale_cache=self.v_scale[i], max_seqlen_k=self.ctx)
-        ops.linear_into(self.attn, [L.o.trellis], [L.o.suh], [L.o.svh], s.bits_o, mcg, mul1, self.residual, ops.Y_ADD)
+        self._row_parallel(self.attn, L.o, s.bits_o)
         rmsnorm(self.residual, L.norm_post, s.eps, out=self.h)
         ops.linear_into(self.h, [L.gate.trellis, L.up.trellis], [L.gate.suh, L.up.suh], [L.gate.svh, L.up.svh],
                         s.bits_gate_up, mcg, mul1, self.act, ops.ACT_SILU_MUL)
-        ops.linear_into(self.act, [L.down.trellis], [L.down.suh], [L.down.svh], s.bits_down, mcg, mul1,
-                        self.residual, ops.Y_ADD)
+        self._row_parallel(self.act, L.down, s.bits_down)
+
+    def _row_parallel(self, x: torch.Tensor, w: Exl3Weight, K: int) -> None:
+        """residual += x @ W: the residual add in the GEMV epilogue; under tensor parallelism the
+        ranks' partial sums are reduced inside the same kernel first."""
+        if self.tp == 1:
+            ops.linear_into(x, [w.trellis], [w.suh], [w.svh], K, *CB, self.residual, ops.Y_ADD)
+        else:
+            from .tp import linear_tp
+            linear_tp(x, w.trellis, w.suh, w.svh, K, *CB, self.comm, residual=self.residual)
 
     def step(self, tokens: torch.Tensor) -> torch.Tensor:
         """One decode step for the M input tokens (int64 on the device); returns the greedy next tokens
@@ -199,7 +270,18 @@ class SyntheticDecoder:
             self.layer_forward(i)
         rmsnorm(self.residual, self.norm_final, s.eps, out=self.h)
         ops.linear_into(self.h, [self.head.trellis], [self.head.suh], [self.head.svh], s.bits_head, *CB, self.logits)
-        torch.argmax(self.logits, dim=-1, out=self.next_tokens)
+        if self.tp == 1:
+            torch.argmax(self.logits, dim=-1, out=self.next_tokens)
+        else:
+            # each rank's best column, then the best over ranks (the first on ties, as one argmax over
+            # the whole vocabulary: ranks hold increasing column ranges)
+            val, idx = torch.max(self.logits, dim=-1)
+            self.pick[:, 0] = val.float()
+            self.pick[:, 1] = (idx + self.v0).float()  # exact: vocab < 2^24
+            torch.distributed.all_gather_into_tensor(self.picks, self.pick, group=self.group)
+            p = self.picks.view(self.tp, self.M, 2)
+            best = torch.argmax(p[:, :, 0], dim=0)
+            self.next_tokens.copy_(p[:, :, 1].gather(0, best[None, :])[0].long())
         return self.next_tokens
 
     def launches_per_step(self) -> int:
@@ -210,7 +292,7 @@ class SyntheticDecoder:
 
 def main(argv=None) -> None:
     """python -m exl3rocm.synthetic [--batch B] [--q-len Q] [--ctx N] [--layers L] [--steps S]
-    Times CUDA-graph replays of the decode step and prints one JSON line."""
+    Times CUDA-graph replays of the decode step on one GPU and prints one JSON line."""
     import argparse
     import json
     ap = argparse.ArgumentParser()
