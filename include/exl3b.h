@@ -117,6 +117,17 @@ EXL3B_API int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, 
                          const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* exl3b_linear_grouped with the RMSNorm before it fused in (vLLM rms_norm): the groups run on
+ *   h = fp16( fp16(x * rsqrt(mean(x^2) + eps)) * norm_weight )      (mean in fp32, per row)
+ * where x [m][k] is the un-normalised input (the residual stream).  norm_weight fp16 [k].  Rows stay
+ * independent of m.  No reference counterpart: the reference runs the norm as a separate vLLM op
+ * before the EXL3 linear. */
+EXL3B_API int exl3b_linear_grouped_rmsnorm(const uint16_t* x, int m, int k, int groups,
+                                 const uint16_t* const* trellis, const int* n, int K, int codebook,
+                                 const uint16_t* norm_weight, float eps, const uint16_t* const* suh,
+                                 const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Paged KV cache, head size 128.  Caches are [num_blocks][block_size][num_kv_heads][row] with
  * row = 128 int8 (int8) or 64 bytes of nibbles (int4: element 2i in the low nibble of byte i),
@@ -134,6 +145,18 @@ EXL3B_API int exl3b_kv_int8_write(const void* key, const void* value, int dtype,
                                   int64_t v_stride_tok, int64_t v_stride_head, int8_t* key_cache,
                                   int8_t* value_cache, float* k_scale, float* v_scale, const int64_t* slot_mapping,
                                   int block_size, void* stream);
+
+/* exl3b_kv_int8_write fused with the neox rotary embedding of the same tokens (exl3b_rope_neox):
+ * row t of qkv (fp16, stride ld) holds num_q_heads q heads, then num_kv_heads k heads, then
+ * num_kv_heads v heads of 128.  q is written rotated to q_out (stride ld_q); k is rotated, rounded to
+ * fp16 and quantised, v quantised, into the int8 caches, byte-identical to exl3b_rope_neox followed
+ * by exl3b_kv_int8_write.  qkv itself is not modified.  No reference counterpart (vLLM runs rotary
+ * embedding and the cache write as separate ops). */
+EXL3B_API int exl3b_kv_int8_write_rope(const uint16_t* qkv, int64_t ld, uint16_t* q_out, int64_t ld_q,
+                             int64_t num_tokens, int num_q_heads, int num_kv_heads, const int64_t* positions,
+                             const float* cos_sin, int64_t max_position, int8_t* key_cache, int8_t* value_cache,
+                             float* k_scale, float* v_scale, const int64_t* slot_mapping, int block_size,
+                             void* stream);
 
 /* int4 quantize-on-write: y = H (x * signs) unnormalised (+ optional rotated-domain bias [heads][128]),
  * 3x3 clip search, asymmetric 4 bit, nibble packing.  With exact_tag != NULL also keeps exact fp16 y

@@ -36,6 +36,7 @@ constexpr int kDecodeWarps = 16;
 constexpr int kProducerWarp = kDecodeWarps;
 constexpr int kThreads = (kDecodeWarps + 1) * 32;
 constexpr int kFlushBar = 1;      // named barrier of the decode warps
+constexpr int kNormBar = 2;       // named barrier of all warps after the fused RMSNorm's row sums
 constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summing them
 constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
 constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
@@ -71,6 +72,10 @@ struct GemvParams {
     int sb_cols;          // widest super-block of the call, in columns
     int64_t ldy;
     int y_add;            // y += result (the residual add of the caller's block)
+    // fused RMSNorm of x (norm_w != null): the linear runs on fp16(fp16(x * s) * norm_w) with
+    // s = rsqrt(mean(x^2) + norm_eps) per row
+    const __half* norm_w;
+    float norm_eps;
     // SwiGLU epilogue (act): groups 0 and 1 (gate, up) of equal width stage their fp16 outputs in
     // `stage` [m][2n]; the second finisher of column block b writes silu(gate) * up to y[0]
     int act;
@@ -145,7 +150,8 @@ struct GemvSmem {
     static constexpr int kAccOffset = kStages * kStageBytes;
     static constexpr int kBarOffset = kAccOffset + kAccBytes;  // full[S], empty[S]
     static constexpr int kFlagOffset = kBarOffset + 2 * kStages * 8;
-    static constexpr int kTotal = kFlagOffset + 16;
+    static constexpr int kNormOffset = kFlagOffset + 16;      // fused RMSNorm: 1/rms of each row
+    static constexpr int kTotal = kNormOffset + 4 * EXL3B_GEMV_MAX_ROWS;
 };
 
 // One decode warp finishes column block `blk` of super-block `sb` (only when a CTA leaves a
@@ -306,6 +312,47 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
     }
 }
 
+// Four inputs of row `row` starting at column col, as fp16 (bf16 x rounded to nearest even, as
+// torch's .to(float16))
+EXL3B_DEV uint2 load_x4(const GemvParams& p, int row, int col) {
+    uint2 xr = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + (int64_t)row * p.k + col);
+    if (p.x_bf16) {
+        const __nv_bfloat162 b01 = *reinterpret_cast<const __nv_bfloat162*>(&xr.x);
+        const __nv_bfloat162 b23 = *reinterpret_cast<const __nv_bfloat162*>(&xr.y);
+        xr.x = h2_as_u32(__floats2half2_rn(__low2float(b01), __high2float(b01)));
+        xr.y = h2_as_u32(__floats2half2_rn(__low2float(b23), __high2float(b23)));
+    }
+    return xr;
+}
+
+// Fused RMSNorm, first half: every thread of the CTA sums the squares of the fp16 inputs of chunks
+// threadIdx.x, threadIdx.x + kThreads, ... (4 inputs each) of each row; warp w's sums go to
+// part[16 w + row].  The split of a row over threads is fixed, so its sum does not depend on m.
+constexpr int kNormChunks = 8;  // 4-input chunks per thread and row: k <= 8 * 4 * kThreads = 17408
+EXL3B_DEV void norm_partials(const GemvParams& p, float* part, int warp, int lane) {
+    const int nch = p.k / 4;
+    for (int row = 0; row < p.m; ++row) {
+        uint2 xr[kNormChunks];  // all of the row's loads in flight together
+#pragma unroll
+        for (int j = 0; j < kNormChunks; ++j) {
+            const int ch = threadIdx.x + j * kThreads;
+            xr[j] = ch < nch ? load_x4(p, row, 4 * ch) : make_uint2(0u, 0u);
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kNormChunks; ++j) {
+            const float2 a = __half22float2(u32_as_h2(xr[j].x)), b = __half22float2(u32_as_h2(xr[j].y));
+            ss = fmaf(a.x, a.x, ss);
+            ss = fmaf(a.y, a.y, ss);
+            ss = fmaf(b.x, b.x, ss);
+            ss = fmaf(b.y, b.y, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        if (lane == 0) part[16 * warp + row] = ss;
+    }
+}
+
 template <int K, int CB, int MT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     using S = GemvSmem<K, MT>;
@@ -317,6 +364,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const uint32_t sbase = smem_u32(smem);
     const uint32_t full0 = sbase + S::kBarOffset, empty0 = full0 + kStages * 8;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kFlagOffset);
+    float* inv_rms = reinterpret_cast<float*>(smem + S::kNormOffset);
+    // the fused RMSNorm's per-warp row sums borrow the accumulator tile: no flush can write it before
+    // the producer has read them (the first flush follows the first published unit)
+    float* norm_part = reinterpret_cast<float*>(smem + S::kAccOffset);
 
     const int c = blockIdx.x, P = p.ctas, U = p.units, ku = p.ku, m = p.m;
     const int u0 = unit_start(c, U, P), u1 = unit_start(c + 1, U, P);
@@ -383,15 +434,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                 const int kt = blk * 8 + ktl;  // this lane's k-tile
                 const bool mine = kt >= kr0 && kt < kr0 + R;
                 const uint2 sr = *reinterpret_cast<const uint2*>(p.suh[si.g] + col);
+                uint2 nw = make_uint2(0u, 0u);
+                if (p.norm_w) nw = *reinterpret_cast<const uint2*>(p.norm_w + col);
                 uint32_t* dst = reinterpret_cast<uint32_t*>(smem + (i % kStages) * S::kStageBytes + S::kTrellisStage +
                                                             (kt - kr0) * m * 32) + (fslot >> 1);
                 for (int row = 0; row < m; ++row) {
-                    uint2 xr = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + (int64_t)row * p.k + col);
-                    if (p.x_bf16) {  // bf16 -> fp16, round to nearest even (torch's .to(float16))
-                        const __nv_bfloat162 b01 = *reinterpret_cast<const __nv_bfloat162*>(&xr.x);
-                        const __nv_bfloat162 b23 = *reinterpret_cast<const __nv_bfloat162*>(&xr.y);
-                        xr.x = h2_as_u32(__floats2half2_rn(__low2float(b01), __high2float(b01)));
-                        xr.y = h2_as_u32(__floats2half2_rn(__low2float(b23), __high2float(b23)));
+                    uint2 xr = load_x4(p, row, col);
+                    if (p.norm_w) {  // RMSNorm: fp16(fp16(x * s) * w), as exl3b_rmsnorm
+                        const float sc = inv_rms[row];
+                        const float2 a = __half22float2(u32_as_h2(xr.x)), b = __half22float2(u32_as_h2(xr.y));
+                        xr.x = h2_as_u32(__hmul2(__floats2half2_rn(a.x * sc, a.y * sc), u32_as_h2(nw.x)));
+                        xr.y = h2_as_u32(__hmul2(__floats2half2_rn(b.x * sc, b.y * sc), u32_as_h2(nw.y)));
                     }
                     const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
                     const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
@@ -411,6 +464,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         const int early = min(nunits, 2);
         for (int i = 0; live && i < early; ++i) live = issue(i);
         griddep_wait();  // x may come from the previous kernel
+        if (p.norm_w) {
+            norm_partials(p, norm_part, warp, lane);
+            named_bar(kNormBar, kThreads);
+            if (lane < m) {  // warps summed in a fixed order
+                float t = 0.f;
+                for (int w = 0; w <= kDecodeWarps; ++w) t += norm_part[16 * w + lane];
+                inv_rms[lane] = rsqrtf(t / (float)p.k + p.norm_eps);
+            }
+            __syncwarp();
+        }
         for (int i = 0; live && i < nunits; ++i) {
             if (i >= early) live = issue(i);
             if (!live) break;
@@ -435,6 +498,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     float* acc_s = reinterpret_cast<float*>(smem + S::kAccOffset);
 
     // ------------------------------ decode warps ------------------------------
+    if (p.norm_w) {  // the fused RMSNorm's row sums, shared with the producer
+        griddep_wait();
+        norm_partials(p, norm_part, warp, lane);
+        named_bar(kNormBar, kThreads);
+    }
     LaneGeom<K> geom;
     geom.init(lane);
     const int gq = lane >> 2, tq = lane & 3;
@@ -716,7 +784,8 @@ static cudaError_t launch_gemv_k(int K, const GemvParams& p, cudaStream_t st) {
 
 int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis, const int* n,
                 int K, int codebook, const uint16_t* const* suh, const uint16_t* const* svh, uint16_t* const* y,
-                int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm) {
+                int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm,
+                const uint16_t* norm_w, float norm_eps) {
     const bool x_bf16 = (codebook & EXL3B_X_BF16) != 0;
     const bool act = (codebook & EXL3B_ACT_SILU_MUL) != 0;
     const bool y_add = (codebook & EXL3B_Y_ADD) != 0;
@@ -727,6 +796,8 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     if (k <= 0 || k % 128) return EXL3B_DECLINED;
     if (!x || !trellis || !n || !suh || !svh || !y || !workspace) return EXL3B_BAD_ARG;
     if (!aligned(x, 8) || k % 4 || ldy % 4 || !aligned(workspace, 256)) return EXL3B_BAD_ARG;
+    if (norm_w && (!aligned(norm_w, 8) || !(norm_eps >= 0.f))) return EXL3B_BAD_ARG;
+    if (norm_w && k > kNormChunks * 4 * kThreads) return EXL3B_DECLINED;
     int64_t n_total = 0;
     for (int g = 0; g < groups; ++g) {
         if (n[g] <= 0 || n[g] % 128) return EXL3B_DECLINED;
@@ -788,6 +859,8 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     p.sb_cols = q.sb_cols;
     p.ldy = ldy;
     p.y_add = y_add ? 1 : 0;
+    p.norm_w = reinterpret_cast<const __half*>(norm_w);
+    p.norm_eps = norm_eps;
     p.act = act ? 1 : 0;
     p.stage = reinterpret_cast<__half*>(ws + L.stage);
     p.act_ctr = blk;
@@ -833,7 +906,8 @@ extern "C" int exl3b_linear(const uint16_t* x, int m, int k, const uint16_t* tre
     const uint16_t* sv[1] = {svh};
     uint16_t* yy[1] = {y};
     int nn[1] = {n};
-    return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, workspace, workspace_bytes, stream, nullptr);
+    return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, workspace, workspace_bytes, stream, nullptr,
+                       nullptr, 0.f);
 }
 
 extern "C" int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis,
@@ -841,7 +915,17 @@ extern "C" int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups,
                                     const uint16_t* const* svh, uint16_t* const* y, int64_t ldy, void* workspace,
                                     size_t workspace_bytes, void* stream) {
     return linear_impl(x, m, k, groups, trellis, n, K, codebook, suh, svh, y, ldy, workspace, workspace_bytes,
-                       stream, nullptr);
+                       stream, nullptr, nullptr, 0.f);
+}
+
+extern "C" int exl3b_linear_grouped_rmsnorm(const uint16_t* x, int m, int k, int groups,
+                                            const uint16_t* const* trellis, const int* n, int K, int codebook,
+                                            const uint16_t* norm_weight, float eps, const uint16_t* const* suh,
+                                            const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
+                                            void* workspace, size_t workspace_bytes, void* stream) {
+    if (!norm_weight) return EXL3B_BAD_ARG;
+    return linear_impl(x, m, k, groups, trellis, n, K, codebook, suh, svh, y, ldy, workspace, workspace_bytes,
+                       stream, nullptr, norm_weight, eps);
 }
 
 extern "C" size_t exl3b_tp_comm_bytes(int tp_size, int max_blocks, int max_rows) {
@@ -911,7 +995,8 @@ extern "C" int exl3b_linear_tp(const uint16_t* x, int m, int k, const uint16_t* 
     const uint16_t* sv[1] = {svh};
     uint16_t* yy[1] = {y};
     int nn[1] = {n};
-    return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, workspace, workspace_bytes, stream, comm);
+    return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, workspace, workspace_bytes, stream, comm,
+                       nullptr, 0.f);
 }
 
 extern "C" int exl3b_linear_workspace_error(const void* workspace, int* out, void* stream) {

@@ -9,7 +9,8 @@ namespace exl3b {
 
 int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* const* trellis, const int* n, int K,
                 int codebook, const uint16_t* const* suh, const uint16_t* const* svh, uint16_t* const* y,
-                int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm);
+                int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm,
+                const uint16_t* norm_w, float norm_eps);
 
 // The scratch: held by every device that loads the library, shared by all calls on that device.
 // In host code `g_noalloc_scratch` names a host-side stand-in, never the device memory; the
@@ -67,5 +68,5 @@ extern "C" int exl3b_linear_noalloc(const uint16_t* x, int m, int k, const uint1
     uint16_t* yy[1] = {y};
     int nn[1] = {n};
     return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, scratch, EXL3B_NOALLOC_SCRATCH_BYTES,
-                       stream, nullptr);
+                       stream, nullptr, nullptr, 0.f);
 }

@@ -106,8 +106,11 @@ __global__ void __launch_bounds__(256) rope_kernel(__half* qkv, int64_t ld, __ha
         const float2 b = __half22float2(*reinterpret_cast<const __half2*>(src + i + 64));
         const float2 c = *reinterpret_cast<const float2*>(cs + i);
         const float2 s = *reinterpret_cast<const float2*>(cs + 64 + i);
-        *reinterpret_cast<__half2*>(dst + i) = __floats2half2_rn(a.x * c.x - b.x * s.x, a.y * c.y - b.y * s.y);
-        *reinterpret_cast<__half2*>(dst + i + 64) = __floats2half2_rn(b.x * c.x + a.x * s.x, b.y * c.y + a.y * s.y);
+        // o = fma(x, c, -(partner * s)) with the product rounded first: one fixed rounding sequence
+        *reinterpret_cast<__half2*>(dst + i) = __floats2half2_rn(__fmaf_rn(a.x, c.x, -__fmul_rn(b.x, s.x)),
+                                                                 __fmaf_rn(a.y, c.y, -__fmul_rn(b.y, s.y)));
+        *reinterpret_cast<__half2*>(dst + i + 64) = __floats2half2_rn(__fmaf_rn(b.x, c.x, __fmul_rn(a.x, s.x)),
+                                                                      __fmaf_rn(b.y, c.y, __fmul_rn(a.y, s.y)));
     }
 }
 

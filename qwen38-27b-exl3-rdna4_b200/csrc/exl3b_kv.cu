@@ -102,6 +102,69 @@ __global__ void kv_int8_write_kernel(const KvWriteArgs a) {
     int8_quant_store(xv, reinterpret_cast<int8_t*>(a.value_cache) + row * kHD, a.v_scale + row, lane);
 }
 
+// The same write fused with the neox rotary embedding of the token's q and k (a decode step's qkv
+// projection output goes straight to the cache): one warp per (token, head slot); slots [0, nq)
+// rotate q head j into q_out, slots [nq, nq + H) rotate k head h, round it to fp16 (the value the
+// unfused route stores), quantise it and v.  Lane l owns elements 4l..4l+3, so the rotation
+// partner of element i (i +- 64) sits in lane l ^ 16.  Rotation arithmetic as exl3b_rope_neox.
+struct KvRopeArgs {
+    const __half* qkv; int64_t ld;      // row t: q heads, k heads, v heads of 128
+    __half* q_out; int64_t ld_q;
+    int nq;
+    const int64_t* positions; const float* cos_sin; int64_t max_pos;
+};
+
+EXL3B_DEV void rope4(float (&x)[4], const float* cs, int lane) {
+    const bool hi = lane >= 16;  // elements 64.. : o = x c + partner s; below: o = x c - partner s
+    const int i0 = (4 * lane) & 63;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float y = __shfl_xor_sync(0xFFFFFFFFu, x[e], 16);
+        const float c = cs[i0 + e], sn = cs[64 + i0 + e];
+        x[e] = hi ? __fmaf_rn(x[e], c, __fmul_rn(y, sn)) : __fmaf_rn(x[e], c, -__fmul_rn(y, sn));
+    }
+}
+
+__global__ void kv_int8_write_rope_kernel(const KvWriteArgs a, const KvRopeArgs r) {
+    const int slots = r.nq + a.num_heads;
+    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= (int64_t)a.num_tokens * slots) return;
+    const int lane = threadIdx.x & 31;
+    const int t = (int)(item / slots), j = (int)(item % slots);
+    const int64_t p = r.positions[t];
+    const bool ok = p >= 0 && p < r.max_pos;
+    const float* cs = r.cos_sin + (ok ? p : 0) * 128;
+    const __half* row_in = r.qkv + t * r.ld;
+    if (j < r.nq) {
+        const uint2 w = *reinterpret_cast<const uint2*>(row_in + j * kHD + 4 * lane);
+        float x[4] = {__low2float(u32_as_h2(w.x)), __high2float(u32_as_h2(w.x)), __low2float(u32_as_h2(w.y)),
+                      __high2float(u32_as_h2(w.y))};
+        rope4(x, cs, lane);
+        uint2 o = make_uint2(h2_as_u32(__floats2half2_rn(x[0], x[1])), h2_as_u32(__floats2half2_rn(x[2], x[3])));
+        if (!ok) o = make_uint2(0u, 0u);
+        *reinterpret_cast<uint2*>(r.q_out + t * r.ld_q + j * kHD + 4 * lane) = o;
+        return;
+    }
+    const int h = j - r.nq;
+    const int64_t slot = a.slot_mapping[t];
+    if (slot < 0) return;
+    const int64_t blk = slot / a.block_size, off = slot % a.block_size;
+    const int64_t row = (blk * a.block_size + off) * a.num_heads + h;
+    const uint2 wk = *reinterpret_cast<const uint2*>(row_in + (r.nq + h) * kHD + 4 * lane);
+    const uint2 wv = *reinterpret_cast<const uint2*>(row_in + (r.nq + a.num_heads + h) * kHD + 4 * lane);
+    float xk[4] = {__low2float(u32_as_h2(wk.x)), __high2float(u32_as_h2(wk.x)), __low2float(u32_as_h2(wk.y)),
+                   __high2float(u32_as_h2(wk.y))};
+    const float xv[4] = {__low2float(u32_as_h2(wv.x)), __high2float(u32_as_h2(wv.x)), __low2float(u32_as_h2(wv.y)),
+                         __high2float(u32_as_h2(wv.y))};
+    if (ok) {
+        rope4(xk, cs, lane);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xk[e] = __half2float(__float2half_rn(xk[e]));
+    }
+    int8_quant_store(xk, reinterpret_cast<int8_t*>(a.key_cache) + row * kHD, a.k_scale + row, lane);
+    int8_quant_store(xv, reinterpret_cast<int8_t*>(a.value_cache) + row * kHD, a.v_scale + row, lane);
+}
+
 // ---------------------------------------------------------------------------------------------
 // int4 write: one warp per (token, KV head, side); RHT in registers, clip search, pack, exact rows
 // ---------------------------------------------------------------------------------------------
@@ -1015,6 +1078,35 @@ extern "C" int exl3b_kv_int8_write(const void* key, const void* value, int dtype
     if (st != EXL3B_OK || num_tokens == 0) return st;
     const int64_t items = num_tokens * num_kv_heads;
     kv_int8_write_kernel<<<(unsigned)((items + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a);
+    return cuda_status(cudaGetLastError());
+}
+
+extern "C" int exl3b_kv_int8_write_rope(const uint16_t* qkv, int64_t ld, uint16_t* q_out, int64_t ld_q,
+                                        int64_t num_tokens, int num_q_heads, int num_kv_heads,
+                                        const int64_t* positions, const float* cos_sin, int64_t max_position,
+                                        int8_t* key_cache, int8_t* value_cache, float* k_scale, float* v_scale,
+                                        const int64_t* slot_mapping, int block_size, void* stream) {
+    if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads <= 0 || max_position < 1) return EXL3B_BAD_ARG;
+    if (num_tokens == 0) return EXL3B_OK;
+    if (!qkv || !positions || !cos_sin || !key_cache || !value_cache || !k_scale || !v_scale || !slot_mapping ||
+        (num_q_heads && !q_out))
+        return EXL3B_BAD_ARG;
+    if (ld < (int64_t)(num_q_heads + 2 * num_kv_heads) * kHD || ld % 4 || (num_q_heads && (ld_q < num_q_heads * kHD || ld_q % 4)))
+        return EXL3B_BAD_ARG;
+    if (!aligned(qkv, 8) || (q_out && !aligned(q_out, 8)) || !aligned(cos_sin, 4) || !aligned(key_cache, 4) ||
+        !aligned(value_cache, 4))
+        return EXL3B_BAD_ARG;
+    if (block_size <= 0) return EXL3B_BAD_ARG;
+    KvWriteArgs a = {};
+    a.key_cache = key_cache; a.value_cache = value_cache; a.k_scale = k_scale; a.v_scale = v_scale;
+    a.slot_mapping = slot_mapping; a.num_tokens = (int)num_tokens; a.num_heads = num_kv_heads;
+    a.block_size = block_size;
+    KvRopeArgs r = {};
+    r.qkv = reinterpret_cast<const __half*>(qkv); r.ld = ld;
+    r.q_out = reinterpret_cast<__half*>(q_out); r.ld_q = ld_q; r.nq = num_q_heads;
+    r.positions = positions; r.cos_sin = cos_sin; r.max_pos = max_position;
+    const int64_t items = num_tokens * (num_q_heads + num_kv_heads);
+    kv_int8_write_rope_kernel<<<(unsigned)((items + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a, r);
     return cuda_status(cudaGetLastError());
 }
 

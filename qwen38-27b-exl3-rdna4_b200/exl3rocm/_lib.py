@@ -43,10 +43,15 @@ SIGNATURES = {
     "exl3b_linear_grouped": (i32, [c_vp, i32, i32, i32, ctypes.POINTER(c_vp), ctypes.POINTER(i32), i32, i32,
                                    ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), i64, c_vp, sz,
                                    c_vp]),
+    "exl3b_linear_grouped_rmsnorm": (i32, [c_vp, i32, i32, i32, ctypes.POINTER(c_vp), ctypes.POINTER(i32), i32, i32,
+                                           c_vp, f32, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp),
+                                           ctypes.POINTER(c_vp), i64, c_vp, sz, c_vp]),
     "exl3b_linear_workspace_error": (i32, [c_vp, ctypes.POINTER(i32), c_vp]),
     "exl3b_linear_noalloc": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp]),
     "exl3b_kv_int8_write": (i32, [c_vp, c_vp, i32, i64, i32, i32, i64, i64, i64, i64, c_vp, c_vp, c_vp, c_vp, c_vp,
                                   i32, c_vp]),
+    "exl3b_kv_int8_write_rope": (i32, [c_vp, i64, c_vp, i64, i64, i32, i32, c_vp, c_vp, i64, c_vp, c_vp, c_vp, c_vp,
+                                       c_vp, i32, c_vp]),
     "exl3b_kv_int4_write": (i32, [c_vp, c_vp, i32, i64, i32, i32, i64, i64, i64, i64, c_vp, c_vp, c_vp, c_vp, c_vp,
                                   i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, i32, c_vp, c_vp, c_vp, c_vp]),
     "exl3b_tp_comm_bytes": (sz, [i32, i32, i32]),

@@ -146,6 +146,24 @@ def reshape_and_cache_int8(key, value, key_cache, value_cache, slot_mapping, k_s
               key_cache.shape[1], _stream(key.device))
 
 
+def rope_and_cache_int8(qkv, q_out, num_q_heads, num_kv_heads, positions, cos_sin, key_cache, value_cache,
+                        slot_mapping, k_scale_cache, v_scale_cache):
+    """Neox RoPE of q (into q_out) and k, then the int8 write of k and v, in one launch: qkv rows
+    [T, (q + 2 kv) heads x 128] fp16, positions int64 [T], cos_sin fp32 [max_pos][128]
+    (exl3b_kv_int8_write_rope; byte-identical to glue.rope_neox + reshape_and_cache_int8)."""
+    assert qkv.dtype == q_out.dtype == torch.float16 and qkv.stride(-1) == 1 and q_out.stride(-1) == 1
+    assert positions.dtype == torch.int64 and cos_sin.dtype == torch.float32
+    n = min(qkv.shape[0], slot_mapping.shape[0])
+    if n == 0:
+        return
+    assert key_cache.is_contiguous() and value_cache.is_contiguous() and k_scale_cache.is_contiguous()
+    slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+    _lib.call("exl3b_kv_int8_write_rope", qkv.data_ptr(), qkv.stride(0), q_out.data_ptr(), q_out.stride(0), n,
+              num_q_heads, num_kv_heads, positions.data_ptr(), cos_sin.data_ptr(), cos_sin.shape[0],
+              key_cache.data_ptr(), value_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(),
+              slots.data_ptr(), key_cache.shape[1], _stream(qkv.device))
+
+
 def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, *, k_scale_cache, v_scale_cache,
                       layer_name=None, query_start_loc=None, seq_lens=None):
     """int4 write (kv_int4.py:176-213): rotate, clip-search quantise, pack; exact rows when the layer

@@ -128,35 +128,39 @@ def had_r_128(inp: torch.Tensor, out: torch.Tensor, pre: Optional[torch.Tensor],
 
 
 def linear_into(x2: torch.Tensor, trellis: list, suh: list, svh: list, K: int, mcg: bool, mul1: bool,
-                y: torch.Tensor, flags: int = 0) -> None:
+                y: torch.Tensor, flags: int = 0, norm: Optional[tuple] = None) -> None:
     """Fused M <= 16 linear of groups sharing x and K; group i -> its column slice of y.  x2 is fp16,
     or bf16 (rounded to fp16 inside the kernel, as the reference's cast at the op boundary).
-    flags: Y_ADD (y += result) or ACT_SILU_MUL (two groups; y receives the activation)."""
+    flags: Y_ADD (y += result) or ACT_SILU_MUL (two groups; y receives the activation).
+    norm = (weight, eps): x2 is the un-normalised input and the RMSNorm runs inside the kernel."""
     M, k = x2.shape
     ng = len(trellis)
     widths = [int(s.shape[0]) for s in svh]
     ws = reserve_workspace(x2.device, k, sum(widths), ng, max(M, 1))
     st = _stream(x2.device)
     cb = _cb(mcg, mul1) | (X_BF16 if x2.dtype == torch.bfloat16 else 0) | flags
-    if flags & ACT_SILU_MUL:
-        assert ng == 2 and widths[0] == widths[1] and y.shape[1] == widths[0]
-        vp = _lib.c_vp * 2
-        _lib.call("exl3b_linear_grouped", x2.data_ptr(), M, k, 2, vp(*[t.data_ptr() for t in trellis]),
-                  (_lib.i32 * 2)(*widths), K, cb, vp(*[s.data_ptr() for s in suh]), vp(*[s.data_ptr() for s in svh]),
-                  vp(y.data_ptr(), y.data_ptr()), y.stride(0), ws.data_ptr(), ws.numel(), st)
-        return
-    if ng == 1:
+    if ng == 1 and norm is None:
         _lib.call("exl3b_linear", x2.data_ptr(), M, k, trellis[0].data_ptr(), widths[0], K, cb,
                   suh[0].data_ptr(), svh[0].data_ptr(), y.data_ptr(), y.stride(0), ws.data_ptr(), ws.numel(), st)
         return
     vp = _lib.c_vp * ng
-    cols = [0]
-    for w in widths[:-1]:
-        cols.append(cols[-1] + w)
-    ys = vp(*[y.data_ptr() + 2 * c0 for c0 in cols])
-    _lib.call("exl3b_linear_grouped", x2.data_ptr(), M, k, ng, vp(*[t.data_ptr() for t in trellis]),
-              (_lib.i32 * ng)(*widths), K, cb, vp(*[s.data_ptr() for s in suh]), vp(*[s.data_ptr() for s in svh]),
-              ys, y.stride(0), ws.data_ptr(), ws.numel(), st)
+    if flags & ACT_SILU_MUL:
+        assert ng == 2 and widths[0] == widths[1] and y.shape[1] == widths[0]
+        ys = vp(y.data_ptr(), y.data_ptr())
+    else:
+        cols = [0]
+        for w in widths[:-1]:
+            cols.append(cols[-1] + w)
+        ys = vp(*[y.data_ptr() + 2 * c0 for c0 in cols])
+    args = [vp(*[t.data_ptr() for t in trellis]), (_lib.i32 * ng)(*widths), K, cb]
+    tail = [vp(*[s.data_ptr() for s in suh]), vp(*[s.data_ptr() for s in svh]), ys, y.stride(0), ws.data_ptr(),
+            ws.numel(), st]
+    if norm is None:
+        _lib.call("exl3b_linear_grouped", x2.data_ptr(), M, k, ng, *args, *tail)
+    else:
+        w, eps = norm
+        assert w.dtype == torch.float16 and w.is_contiguous() and w.shape[0] == k
+        _lib.call("exl3b_linear_grouped_rmsnorm", x2.data_ptr(), M, k, ng, *args, w.data_ptr(), float(eps), *tail)
 
 
 def _prep_x(x: torch.Tensor, k: int, keep_bf16: bool = False) -> torch.Tensor:

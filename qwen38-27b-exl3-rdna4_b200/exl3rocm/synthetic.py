@@ -11,10 +11,13 @@ checkpoint (a hybrid model with linear-attention layers) is not available here; 
 for its full-attention layers.
 
 One step (``step``) runs, for M = batch * q_len query rows:
-  embed -> 64 x [ rmsnorm -> qkv (one grouped launch) -> rope (q out, k in place) -> int8 KV write
-  -> paged int8 attention -> o (+ residual in the epilogue) -> rmsnorm -> gate/up with SiLU * up
-  in the epilogue -> down (+ residual in the epilogue) ] -> rmsnorm -> lm_head -> argmax
-All buffers are allocated up front, so the step can be captured in a CUDA graph.
+  embed -> 64 x [ qkv (one grouped launch, the RMSNorm of its input fused in) -> rope + int8 KV write
+  (one launch) -> paged int8 attention + split combine -> o (+ residual in the epilogue) -> gate/up
+  (RMSNorm fused in, SiLU * up in the epilogue) -> down (+ residual in the epilogue) ]
+  -> lm_head (final RMSNorm fused in) -> argmax
+seven of this library's launches per layer.  fused=False runs the same step with separate RMSNorm,
+RoPE and KV-write launches (ten per layer), for comparison.  All buffers are allocated up front, so
+the step can be captured in a CUDA graph.
 
 Tensor parallel (tp_size > 1, one process per GPU): every rank draws the whole model from the same
 seed, layer by layer, and keeps its shard, so the sharded model is the single-GPU model.  q/k/v
@@ -133,13 +136,14 @@ class SyntheticDecoder:
 
     def __init__(self, shape: DecoderShape, device, batch: int = 1, q_len: int = 1, ctx: int = 32768,
                  seed: int = 0, weights_of: "SyntheticDecoder | None" = None, tp_size: int = 1, tp_rank: int = 0,
-                 comm=None, group=None):
+                 comm=None, group=None, fused: bool = True):
         """weights_of: take the weights of another decoder of the same shape and sharding (a different
         batch, query length or context over the same model)."""
         s = self.s = shape
         self.device = device = torch.device(device)
         self.batch, self.q_len, self.ctx = batch, q_len, ctx
         self.tp, self.rank, self.comm, self.group = tp_size, tp_rank, comm, group
+        self.fused = fused
         M = self.M = batch * q_len
         if M > ops.GEMV_MAX_ROWS:
             raise ValueError(f"decode step of {M} rows: the fused linears take 1..{ops.GEMV_MAX_ROWS}")
@@ -233,24 +237,34 @@ class SyntheticDecoder:
         s, L = self.s, self.layers[i]
         qd, kd, M = self.hq * s.head, self.hkv * s.head, self.M
         mcg, mul1 = CB
-        rmsnorm(self.residual, L.norm_in, s.eps, out=self.h)
-        ops.linear_into(self.h, [L.q.trellis, L.k.trellis, L.v.trellis], [L.q.suh, L.k.suh, L.v.suh],
-                        [L.q.svh, L.k.svh, L.v.svh], s.bits_qkv, mcg, mul1, self.qkv)
-        rope_neox(self.qkv, self.q, self.hq, self.hkv, self.positions, self.cos_sin)
-        key = self.qkv[:, qd:qd + kd].view(M, self.hkv, s.head)
-        val = self.qkv[:, qd + kd:].view(M, self.hkv, s.head)
-        kv.reshape_and_cache_int8(key, val, self.k_cache[i], self.v_cache[i], self.slot_mapping, self.k_scale[i],
-                                  self.v_scale[i])
+        self._normed_linear(L.norm_in, [L.q, L.k, L.v], s.bits_qkv, self.qkv)
+        if self.fused:
+            kv.rope_and_cache_int8(self.qkv, self.q, self.hq, self.hkv, self.positions, self.cos_sin,
+                                   self.k_cache[i], self.v_cache[i], self.slot_mapping, self.k_scale[i],
+                                   self.v_scale[i])
+        else:
+            rope_neox(self.qkv, self.q, self.hq, self.hkv, self.positions, self.cos_sin)
+            key = self.qkv[:, qd:qd + kd].view(M, self.hkv, s.head)
+            val = self.qkv[:, qd + kd:].view(M, self.hkv, s.head)
+            kv.reshape_and_cache_int8(key, val, self.k_cache[i], self.v_cache[i], self.slot_mapping,
+                                      self.k_scale[i], self.v_scale[i])
         kv.attention_int8(q=self.q.view(M, self.hq, s.head), k=self.k_cache[i], v=self.v_cache[i],
                           out=self.attn.view(M, self.hq, s.head), cu_seqlens_q=self.cu_q, max_seqlen_q=self.q_len,
                           seqused_k=self.seq_lens, block_table=self.block_table,
                           softmax_scale=1.0 / math.sqrt(s.head), k_scale_cache=self.k_scale[i],
                           v_scale_cache=self.v_scale[i], max_seqlen_k=self.ctx)
         self._row_parallel(self.attn, L.o, s.bits_o)
-        rmsnorm(self.residual, L.norm_post, s.eps, out=self.h)
-        ops.linear_into(self.h, [L.gate.trellis, L.up.trellis], [L.gate.suh, L.up.suh], [L.gate.svh, L.up.svh],
-                        s.bits_gate_up, mcg, mul1, self.act, ops.ACT_SILU_MUL)
+        self._normed_linear(L.norm_post, [L.gate, L.up], s.bits_gate_up, self.act, ops.ACT_SILU_MUL)
         self._row_parallel(self.act, L.down, s.bits_down)
+
+    def _normed_linear(self, norm_w: torch.Tensor, ws: list, K: int, y: torch.Tensor, flags: int = 0) -> None:
+        """y = linear(RMSNorm(residual)): the norm inside the GEMV, or (fused=False) its own launch."""
+        args = ([w.trellis for w in ws], [w.suh for w in ws], [w.svh for w in ws], K, *CB, y, flags)
+        if self.fused:
+            ops.linear_into(self.residual, *args, norm=(norm_w, self.s.eps))
+        else:
+            rmsnorm(self.residual, norm_w, self.s.eps, out=self.h)
+            ops.linear_into(self.h, *args)
 
     def _row_parallel(self, x: torch.Tensor, w: Exl3Weight, K: int) -> None:
         """residual += x @ W: the residual add in the GEMV epilogue; under tensor parallelism the
@@ -268,8 +282,7 @@ class SyntheticDecoder:
         torch.index_select(self.embed, 0, tokens, out=self.residual)
         for i in range(s.layers):
             self.layer_forward(i)
-        rmsnorm(self.residual, self.norm_final, s.eps, out=self.h)
-        ops.linear_into(self.h, [self.head.trellis], [self.head.suh], [self.head.svh], s.bits_head, *CB, self.logits)
+        self._normed_linear(self.norm_final, [self.head], s.bits_head, self.logits)
         if self.tp == 1:
             torch.argmax(self.logits, dim=-1, out=self.next_tokens)
         else:
@@ -285,9 +298,9 @@ class SyntheticDecoder:
         return self.next_tokens
 
     def launches_per_step(self) -> int:
-        """This library's kernel launches in one step: per layer rmsnorm x2, 4 linears, rope, the KV
-        write, the attention and its split combine; then the final norm and the lm_head."""
-        return self.s.layers * 10 + 2
+        """This library's kernel launches in one step: per layer 4 linears (norms fused), rope + KV write,
+        the attention and its split combine, then the lm_head; unfused: 3 more per layer, 1 more at the end."""
+        return self.s.layers * 7 + 1 if self.fused else self.s.layers * 10 + 2
 
 
 def main(argv=None) -> None:
@@ -302,9 +315,11 @@ def main(argv=None) -> None:
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--unfused", action="store_true", help="separate RMSNorm, RoPE and KV-write launches")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
-    dec = SyntheticDecoder(DecoderShape(layers=a.layers), dev, batch=a.batch, q_len=a.q_len, ctx=a.ctx, seed=2024)
+    dec = SyntheticDecoder(DecoderShape(layers=a.layers), dev, batch=a.batch, q_len=a.q_len, ctx=a.ctx, seed=2024,
+                           fused=not a.unfused)
     st = torch.cuda.Stream(dev)
     st.wait_stream(torch.cuda.current_stream(dev))
     dec.reserve(st)
@@ -324,7 +339,8 @@ def main(argv=None) -> None:
         e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.steps
-    print(json.dumps({"batch": a.batch, "q_len": a.q_len, "ctx": a.ctx, "layers": a.layers, "ms_per_step": ms,
+    print(json.dumps({"batch": a.batch, "q_len": a.q_len, "ctx": a.ctx, "layers": a.layers, "fused": dec.fused,
+                      "ms_per_step": ms,
                       "rows_per_s": dec.M / (ms * 1e-3), "weight_bytes": dec.weight_bytes(),
                       "kv_bytes": dec.kv_bytes()}))
     del graph

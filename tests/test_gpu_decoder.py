@@ -122,3 +122,19 @@ def test_decode_step_graph_replay(syn):
         torch.cuda.synchronize()
         assert torch.equal(dec.logits, eager)
     del g
+
+
+def test_fused_step_matches_unfused(syn):
+    """The fused step (RMSNorm inside the GEMVs, RoPE inside the KV write) against the same model run
+    with separate RMSNorm, RoPE and KV-write launches: only the norms' per-row scales may round
+    differently."""
+    shape = syn.DecoderShape(**SMALL)
+    a = syn.SyntheticDecoder(shape, DEV, batch=3, q_len=1, ctx=256, seed=11)
+    b = syn.SyntheticDecoder(shape, DEV, batch=3, q_len=1, ctx=256, seed=11, fused=False)
+    tokens = torch.randint(0, shape.vocab, (a.M,), device=DEV)
+    a.step(tokens)
+    b.step(tokens)
+    got, ref = a.logits.float(), b.logits.float()
+    nrms = float((got - ref).pow(2).mean().sqrt() / ref.pow(2).mean().sqrt())
+    assert nrms <= 2e-3, nrms
+    assert a.launches_per_step() == 7 * shape.layers + 1

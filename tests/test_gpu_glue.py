@@ -151,3 +151,65 @@ def test_rope_neox(mods):
     assert torch.equal(qkv[:, (nq + nk) * 128:], before[:, (nq + nk) * 128:])  # v untouched
     # the table: position 0 is the identity
     assert torch.equal(q[0], before[0, :nq * 128])
+
+
+# reference tests/test_gpu_parity.py:51-52, 65-70 (the linear's gates)
+def _gates(got, ref):
+    g, r = got.double().flatten(), ref.double().flatten()
+    d = g - r
+    scale = float(r.pow(2).mean().sqrt()) or 1.0
+    return (float(d.abs().max()) / scale <= 3e-3 and float(d.pow(2).mean().sqrt()) / scale <= 2e-4
+            and float(torch.nn.functional.cosine_similarity(g, r, dim=0)) >= 0.999999)
+
+
+@pytest.mark.parametrize("groups", [1, 3])
+def test_linear_with_fused_rmsnorm(mods, groups):
+    """The RMSNorm inside the GEMV against exl3b_rmsnorm then the linear: the per-row scale may round
+    differently (another fp32 summation order), so the outputs meet the linear's gates rather than
+    matching bitwise; rows stay bitwise independent of m."""
+    ops, glue = mods
+    k, K, eps = 5120, 4, 1e-6
+    ns = [1024, 256, 256][:groups]
+    ws = [_weights(k, n, K, 40 + i) for i, n in enumerate(ns)]
+    tr, su, sv = [w[0] for w in ws], [w[1] for w in ws], [w[2] for w in ws]
+    nw = (1 + 0.1 * torch.randn(k, device=DEV)).to(torch.float16)
+    x = (torch.randn(5, k, device=DEV) * 2).to(torch.float16)
+    fused = torch.empty(5, sum(ns), dtype=torch.float16, device=DEV)
+    ops.linear_into(x, tr, su, sv, K, False, True, fused, norm=(nw, eps))
+    h = glue.rmsnorm(x, nw, eps)
+    ref = torch.empty_like(fused)
+    ops.linear_into(h, tr, su, sv, K, False, True, ref)
+    torch.cuda.synchronize()
+    assert _gates(fused, ref)
+    one = torch.empty(1, sum(ns), dtype=torch.float16, device=DEV)
+    ops.linear_into(x[3:4], tr, su, sv, K, False, True, one, norm=(nw, eps))
+    assert torch.equal(one[0], fused[3])
+
+
+def test_rope_and_cache_int8_equals_two_kernels(mods):
+    ops, glue = mods
+    from exl3rocm import kv
+    torch.manual_seed(4)
+    T, nq, nkv, bs, nblk, ctx = 7, 40, 8, 16, 64, 1024
+    qkv = torch.randn(T, (nq + 2 * nkv) * 128, device=DEV).to(torch.float16)
+    pos = torch.tensor([0, 5, 100, 1023, 64, 7, 512], dtype=torch.int64, device=DEV)
+    slots = torch.tensor([3, 17, 200, -1, 511, 1000, 64], dtype=torch.int64, device=DEV)
+    cs = glue.rope_cos_sin(ctx, 1e6, DEV)
+
+    def caches():
+        return (torch.zeros(nblk, bs, nkv, 128, dtype=torch.int8, device=DEV),
+                torch.zeros(nblk, bs, nkv, 128, dtype=torch.int8, device=DEV),
+                torch.zeros(nblk, bs, nkv, device=DEV), torch.zeros(nblk, bs, nkv, device=DEV))
+    kc1, vc1, ks1, vs1 = caches()
+    q1 = torch.empty(T, nq * 128, dtype=torch.float16, device=DEV)
+    kv.rope_and_cache_int8(qkv, q1, nq, nkv, pos, cs, kc1, vc1, slots, ks1, vs1)
+    kc2, vc2, ks2, vs2 = caches()
+    q2 = torch.empty_like(q1)
+    work = qkv.clone()
+    glue.rope_neox(work, q2, nq, nkv, pos, cs)
+    kv.reshape_and_cache_int8(work[:, nq * 128:(nq + nkv) * 128].view(T, nkv, 128),
+                              work[:, (nq + nkv) * 128:].view(T, nkv, 128), kc2, vc2, slots, ks2, vs2)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2)
+    for a, b in ((kc1, kc2), (vc1, vc2), (ks1, ks2), (vs1, vs2)):
+        assert torch.equal(a, b)
