@@ -578,7 +578,7 @@ def main():
     if world == 1 and not args.no_extra:
         extra["kv_attention"] = [bench_kv(torch, dev, kind, ctx, b, ql)
                                  for kind, ctx, b, ql in ((8, 32768, 8, 1), (4, 32768, 8, 1), (8, 32768, 1, 4),
-                                                          (4, 65536, 1, 1), (8, 4096, 8, 1))]
+                                                          (4, 65536, 1, 1), (8, 4096, 8, 1), (8, 32768, 1, 1))]
         extra["prefill_m2048"] = bench_prefill(torch, dev, K)
 
     if not args.no_extra and not args.no_decode and (world == 1 or comm is not None):

@@ -404,6 +404,7 @@ EXL3B_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_pe
 // Each warp owns 8 * NT query rows; the CTA's warps share nothing and never wait on one another.
 template <int KV, int NT>
 __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
+    griddep_launch();  // the split combine may be scheduled now; it waits for this grid's partials
     using Tr = KvTraits<KV>;
     using SM = AttnSmem<KV>;
     constexpr int RB = SM::kRowBytes;
@@ -869,13 +870,18 @@ struct KvReduceArgs {
 };
 
 // One CTA per (query token, q head).  The split maxima and row sums are read by one thread per
-// split and reduced over the CTA; warp j then accumulates splits j, j + 8, ... of the weighted
-// outputs and warp 0 sums the eight partial vectors in warp order (a fixed order: deterministic).
-constexpr int kReduceThreads = 256;
+// split and reduced over the CTA; warp j then accumulates splits j, j + 32, ... of the weighted
+// outputs (at most 8 each, all loads in flight together) and warp 0 sums the 32 partial vectors in
+// warp order (a fixed order: deterministic).  A programmatic dependent launch: it is scheduled
+// while the attention runs and waits for its partials.
+constexpr int kReduceThreads = 1024;
 constexpr int kReduceWarps = kReduceThreads / 32;
 static_assert(kMaxSplits <= kReduceThreads, "one thread per split");
+static_assert(kMaxSplits <= 8 * kReduceWarps, "at most 8 splits per warp");
 
 __global__ void __launch_bounds__(kReduceThreads) kv_reduce_kernel(const KvReduceArgs a) {
+    griddep_launch();  // the next kernel (an EXL3 linear) may start streaming its weights
+    griddep_wait();    // the attention's partials
     const int64_t item = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = (int)(item / a.num_q_heads);
@@ -912,12 +918,18 @@ __global__ void __launch_bounds__(kReduceThreads) kv_reduce_kernel(const KvReduc
 #pragma unroll
     for (int i = 0; i < kReduceWarps; ++i) lsum += red_l[i];
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int j = warp; j < nsp; j += kReduceWarps) {
-        const float wj = w_s[j];
-        if (wj == 0.f) continue;
-        const float4 x = reinterpret_cast<const float4*>(base + j * kPartialStride)[lane];
-        v.x += wj * x.x; v.y += wj * x.y; v.z += wj * x.z; v.w += wj * x.w;
+    float4 xs[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int j = warp + i * kReduceWarps;
+        xs[i] = (j < nsp && w_s[j] != 0.f) ? reinterpret_cast<const float4*>(base + j * kPartialStride)[lane]
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int j = warp + i * kReduceWarps;
+        const float wj = j < nsp ? w_s[j] : 0.f;
+        v.x += wj * xs[i].x; v.y += wj * xs[i].y; v.z += wj * xs[i].z; v.w += wj * xs[i].w;
     }
     acc_s[warp][lane] = v;
     __syncthreads();
@@ -1202,8 +1214,16 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     r.query_start_loc = query_start_loc; r.num_seqs = num_seqs; r.num_tokens = num_tokens;
     r.num_q_heads = num_q_heads; r.num_splits = S; r.unrot_signs = kv == 4 ? rht_signs : nullptr;
     const int64_t items = (int64_t)num_tokens * num_q_heads;
-    kv_reduce_kernel<<<(unsigned)items, kReduceThreads, 0, st>>>(r);
-    return cuda_status(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)items);
+    cfg.blockDim = dim3(kReduceThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kv_reduce_kernel, r));
 }
 
 extern "C" int exl3b_kv_int8_attn(const uint16_t* q, uint16_t* out, int num_tokens, int num_q_heads,
