@@ -869,21 +869,20 @@ struct KvReduceArgs {
     const float* unrot_signs;  // int4: RHT signs, else null
 };
 
-// One CTA per (query token, q head).  The split maxima and row sums are read by one thread per
-// split and reduced over the CTA; warp j then accumulates splits j, j + 32, ... of the weighted
-// outputs (at most 8 each, all loads in flight together) and warp 0 sums the 32 partial vectors in
-// warp order (a fixed order: deterministic).  A programmatic dependent launch: it is scheduled
-// while the attention runs and waits for its partials.
-constexpr int kReduceThreads = 1024;
-constexpr int kReduceWarps = kReduceThreads / 32;
-static_assert(kMaxSplits <= kReduceThreads, "one thread per split");
+// One CTA per (query token, q head) of W = ceil(splits / 8) warps (at most 32).  The split maxima
+// and row sums are read by one thread per split and reduced over the CTA; warp j then accumulates
+// splits j, j + W, ... of the weighted outputs (at most 8 each, all loads in flight together) and
+// warp 0 sums the W partial vectors in warp order (a fixed order: deterministic).  A programmatic
+// dependent launch: it is scheduled while the attention runs and waits for its partials.
+constexpr int kReduceWarps = 32;  // most warps a CTA takes
 static_assert(kMaxSplits <= 8 * kReduceWarps, "at most 8 splits per warp");
+static int reduce_warps(int splits) { return std::min(kReduceWarps, std::max(1, (splits + 7) / 8)); }
 
-__global__ void __launch_bounds__(kReduceThreads) kv_reduce_kernel(const KvReduceArgs a) {
+__global__ void __launch_bounds__(32 * kReduceWarps) kv_reduce_kernel(const KvReduceArgs a) {
     griddep_launch();  // the next kernel (an EXL3 linear) may start streaming its weights
     griddep_wait();    // the attention's partials
     const int64_t item = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int t = (int)(item / a.num_q_heads);
     const int s = seq_of_token(a.query_start_loc, a.num_seqs, t);
     const int L = a.seq_lens[s];
@@ -905,8 +904,7 @@ __global__ void __launch_bounds__(kReduceThreads) kv_reduce_kernel(const KvReduc
     if (lane == 0) red_m[warp] = M;
     __syncthreads();
     M = red_m[0];
-#pragma unroll
-    for (int i = 1; i < kReduceWarps; ++i) M = fmaxf(M, red_m[i]);
+    for (int i = 1; i < nw; ++i) M = fmaxf(M, red_m[i]);
     const float w = (ms == -INFINITY) ? 0.f : exp_f(ms - M);  // M is finite when any split is
     float l = w * ls;
 #pragma unroll
@@ -915,19 +913,18 @@ __global__ void __launch_bounds__(kReduceThreads) kv_reduce_kernel(const KvReduc
     if (sp < kMaxSplits) w_s[sp] = w;
     __syncthreads();
     float lsum = 0.f;
-#pragma unroll
-    for (int i = 0; i < kReduceWarps; ++i) lsum += red_l[i];
+    for (int i = 0; i < nw; ++i) lsum += red_l[i];
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 xs[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int j = warp + i * kReduceWarps;
+        const int j = warp + i * nw;
         xs[i] = (j < nsp && w_s[j] != 0.f) ? reinterpret_cast<const float4*>(base + j * kPartialStride)[lane]
                                            : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int j = warp + i * kReduceWarps;
+        const int j = warp + i * nw;
         const float wj = j < nsp ? w_s[j] : 0.f;
         v.x += wj * xs[i].x; v.y += wj * xs[i].y; v.z += wj * xs[i].z; v.w += wj * xs[i].w;
     }
@@ -935,8 +932,7 @@ __global__ void __launch_bounds__(kReduceThreads) kv_reduce_kernel(const KvReduc
     __syncthreads();
     if (warp != 0) return;
     float r[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < kReduceWarps; ++i) {
+    for (int i = 0; i < nw; ++i) {
         const float4 x = acc_s[i][lane];
         r[0] += x.x; r[1] += x.y; r[2] += x.z; r[3] += x.w;
     }
@@ -1216,7 +1212,7 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     const int64_t items = (int64_t)num_tokens * num_q_heads;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)items);
-    cfg.blockDim = dim3(kReduceThreads);
+    cfg.blockDim = dim3(32 * reduce_warps(S));
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
