@@ -37,6 +37,7 @@ constexpr int kProducerWarp = kDecodeWarps;
 constexpr int kThreads = (kDecodeWarps + 1) * 32;
 constexpr int kFlushBar = 1;      // named barrier of the decode warps
 constexpr int kNormBar = 2;       // named barrier of all warps after the fused RMSNorm's row sums
+constexpr int kPairBar0 = 3;      // named barriers 3..10: the two warps that finish column block b
 constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summing them
 constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
 constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
@@ -150,16 +151,27 @@ struct GemvSmem {
     static constexpr int kAccOffset = kStages * kStageBytes;
     static constexpr int kBarOffset = kAccOffset + kAccBytes;  // full[S], empty[S]
     static constexpr int kFlagOffset = kBarOffset + 2 * kStages * 8;
-    static constexpr int kNormOffset = kFlagOffset + 16;      // fused RMSNorm: 1/rms of each row
+    // flags: abort (int), the flush's abort snapshot (int), the finish decision of each column
+    // block shared by its two warps (8 ints)
+    static constexpr int kNormOffset = kFlagOffset + 64;      // fused RMSNorm: 1/rms of each row
     static constexpr int kTotal = kNormOffset + 4 * EXL3B_GEMV_MAX_ROWS;
 };
 
-// One decode warp finishes column block `blk` of super-block `sb` (only when a CTA leaves a
-// super-block).
+// Decode warps blk (half 0) and blk + 8 (half 1) finish column block `blk` of super-block `sb`
+// (only when a CTA leaves a super-block); with m > 1 each takes half of the rows, half 0 the first
+// ceil(m / 2), so twice the partial loads are in flight.  With m == 1 warp blk works alone.  The two
+// warps meet at named barrier kPairBar0 + blk; `fin` is their shared decision word.
 template <int MT>
 __device__ __forceinline__ void flush_block(const GemvParams& p, const float* acc_s, volatile int* abort_flag, int c,
-                                         int sb, SbInfo si, int blk, int u0, int u1, int lane) {
+                                         int sb, SbInfo si, int blk, int half, int u0, int u1, int lane,
+                                         volatile int* fin) {
     const int ku = p.ku, U = p.units, P = p.ctas, m = p.m;
+    const bool pair = m > 1;
+    const int mh = (m + 1) >> 1;
+    const int r_lo = pair ? half * mh : 0, r_hi = pair ? (half ? m : mh) : m;  // this warp's rows
+    auto pair_sync = [&]() {
+        if (pair) named_bar(kPairBar0 + blk, 64);
+    };
     // If this CTA covered the super-block's whole k range, transform and store; otherwise
     // publish the partial and, if it is the last of the block's CTAs to arrive, gather all
     // partials in fixed CTA order and finish the block.
@@ -173,19 +185,25 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
         // CTA ranges are contiguous and ordered, so cta + super-block is unique among the
         // (CTA, super-block) pairs that meet
         float* mine = p.partials + ((int64_t)(c + sb) * m) * p.sb_cols;
-        for (int row = 0; row < m; ++row)
+        for (int row = r_lo; row < r_hi; ++row)
             __stcg(reinterpret_cast<float4*>(mine + (int64_t)row * p.sb_cols + col),
                    *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col));
         __syncwarp();
-        int v = 0;
-        if (lane == 0) {
-            // acq_rel at gpu scope: releases the warp's partial stores (ordered before this by the
-            // __syncwarp) and, for the last arriver, acquires the other CTAs' partials
-            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(v) : "l"(p.counters + Bg) : "memory");
+        pair_sync();  // both halves' partial stores come before the release below
+        if (half == 0) {
+            int v = 0;
+            if (lane == 0) {
+                // acq_rel at gpu scope: releases the pair's partial stores (ordered before this by
+                // the barriers) and, for the last arriver, acquires the other CTAs' partials
+                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(v) : "l"(p.counters + Bg) : "memory");
+                *fin = v;
+            }
+            v = __shfl_sync(0xFFFFFFFFu, v, 0);
+            __syncwarp();  // every lane's loads of the partials below come after lane 0's acquire
+            finalize = (v == cl - cf);
         }
-        v = __shfl_sync(0xFFFFFFFFu, v, 0);
-        __syncwarp();  // every lane's loads of the partials below come after lane 0's acquire
-        finalize = (v == cl - cf);
+        pair_sync();  // half 1 reads the decision after the acquire
+        if (half == 1) finalize = (*fin == cl - cf);
     }
     if (finalize) {
         const int b = si.b0 + blk;
@@ -235,24 +253,31 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
             *dst = make_uint2(h2_as_u32(y01), h2_as_u32(y23));
         };
         if (p.tp_size <= 1) {
-            for (int row = 0; row < m; ++row) {
+            for (int row = r_lo; row < r_hi; ++row) {
                 float v[4];
                 block_sum(row, v);
                 finish_row(row, v);
             }
             if (p.act) {
-                // gate and up block b are finished by different warps, in any order: the second
-                // one (pair counter) reads both staged blocks and writes the activation
+                // gate and up block b are finished by different warp pairs, in any order: the
+                // second one (pair counter) reads both staged blocks and writes the activation
                 __syncwarp();
+                pair_sync();  // both halves' staged rows come before the release below
                 int w = 0;
-                if (lane == 0)
-                    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n"
-                                 : "=r"(w) : "l"(p.counters + p.act_ctr + b) : "memory");
-                w = __shfl_sync(0xFFFFFFFFu, w, 0);
-                __syncwarp();
+                if (half == 0) {
+                    if (lane == 0) {
+                        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n"
+                                     : "=r"(w) : "l"(p.counters + p.act_ctr + b) : "memory");
+                        *fin = w;
+                    }
+                    w = __shfl_sync(0xFFFFFFFFu, w, 0);
+                    __syncwarp();
+                }
+                pair_sync();
+                if (half == 1) w = *fin;
                 if (w == 1) {
                     const int64_t nn = p.g.n_tiles[0] * 16;
-                    for (int row = 0; row < m; ++row) {
+                    for (int row = r_lo; row < r_hi; ++row) {
                         const __half* s = p.stage + (int64_t)row * 2 * nn + b * 128 + 4 * lane;
                         const uint2 g = __ldcg(reinterpret_cast<const uint2*>(s));
                         const uint2 u = __ldcg(reinterpret_cast<const uint2*>(s + nn));
@@ -261,7 +286,7 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
                         *reinterpret_cast<uint2*>(p.g.y[0] + row * p.ldy + b * 128 + 4 * lane) =
                             make_uint2(h2_as_u32(a01), h2_as_u32(a23));
                     }
-                    if (lane == 0) p.counters[p.act_ctr + b] = 0;
+                    if (lane == 0 && half == 0) p.counters[p.act_ctr + b] = 0;
                 }
             }
         } else {
@@ -276,7 +301,7 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
                 return reinterpret_cast<uint32_t*>(p.tp_buf[owner] + kTpHeader) +
                        ((((int64_t)par * tp + src) * nb + b) * rows + row) * 256 + 8 * lane;
             };
-            for (int row = 0; row < m; ++row) {
+            for (int row = r_lo; row < r_hi; ++row) {
                 float v[4];
                 block_sum(row, v);
                 for (int r = 0; r < tp; ++r) {
@@ -286,7 +311,7 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
                 }
             }
             bool ok = true;
-            for (int row = 0; row < m; ++row) {
+            for (int row = r_lo; row < r_hi; ++row) {
                 float v[4] = {0.f, 0.f, 0.f, 0.f};
                 for (int r = 0; r < tp; ++r) {  // fixed rank order: identical sums on every rank
                     const uint32_t* q = slot(rk, r, row);
@@ -308,7 +333,7 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
                 finish_row(row, v);
             }
         }
-        if (!whole && lane == 0) p.counters[Bg] = 0;
+        if (!whole && lane == 0 && half == 0) p.counters[Bg] = 0;
     }
 }
 
@@ -364,6 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const uint32_t sbase = smem_u32(smem);
     const uint32_t full0 = sbase + S::kBarOffset, empty0 = full0 + kStages * 8;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kFlagOffset);
+    volatile int* flush_snap = abort_flag + 1;  // the abort flag as every flushing warp sees it
+    volatile int* fin_s = abort_flag + 2;       // [8] finish decisions of the column-block pairs
     float* inv_rms = reinterpret_cast<float*>(smem + S::kNormOffset);
     // the fused RMSNorm's per-warp row sums borrow the accumulator tile: no flush can write it before
     // the producer has read them (the first flush follows the first published unit)
@@ -645,9 +672,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
             }
+        if (threadIdx.x == 0) *flush_snap = *abort_flag;  // both warps of a pair must agree to enter
         named_bar(kFlushBar, kDecodeWarps * 32);
-        if (warp < si.nblk && *abort_flag == 0)
-            flush_block<MT>(p, acc_s, abort_flag, c, sb, si, warp, u0, u1, lane);
+        {
+            const int fb = warp & 7, half = warp >> 3;
+            if (fb < si.nblk && (half == 0 || m > 1) && *flush_snap == 0)
+                flush_block<MT>(p, acc_s, abort_flag, c, sb, si, fb, half, u0, u1, lane, fin_s + fb);
+        }
         if (i + 1 < nunits) {
             ++sb;
             si = sb_info(p.g, p.groups, sb);
