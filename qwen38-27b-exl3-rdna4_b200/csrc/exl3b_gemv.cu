@@ -465,28 +465,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                 if (p.norm_w) nw = *reinterpret_cast<const uint2*>(p.norm_w + col);
                 uint32_t* dst = reinterpret_cast<uint32_t*>(smem + (i % kStages) * S::kStageBytes + S::kTrellisStage +
                                                             (kt - kr0) * m * 32) + (fslot >> 1);
-                for (int r0 = 0; r0 < m; r0 += 4) {
-                    uint2 xg[4];  // four rows' loads in flight together
+                auto one_row = [&](int row, uint2 xr) {
+                    if (p.norm_w) {  // RMSNorm: fp16(fp16(x * s) * w), as exl3b_rmsnorm
+                        const float sc = inv_rms[row];
+                        const float2 a = __half22float2(u32_as_h2(xr.x)), b = __half22float2(u32_as_h2(xr.y));
+                        xr.x = h2_as_u32(__hmul2(__floats2half2_rn(a.x * sc, a.y * sc), u32_as_h2(nw.x)));
+                        xr.y = h2_as_u32(__hmul2(__floats2half2_rn(b.x * sc, b.y * sc), u32_as_h2(nw.y)));
+                    }
+                    const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
+                    const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
+                    float v[4] = {__low2float(p01), __high2float(p01), __low2float(p23), __high2float(p23)};
+                    had128_warp(v);
+                    if (mine) {
+                        dst[row * 8] = h2_as_u32(__floats2half2_rn(v[0] * kRScale, v[1] * kRScale));
+                        dst[row * 8 + 2] = h2_as_u32(__floats2half2_rn(v[2] * kRScale, v[3] * kRScale));
+                    }
+                };
+                if (m == 1) {
+                    one_row(0, load_x4(p, 0, col));
+                } else {
+                    for (int r0 = 0; r0 < m; r0 += 4) {
+                        uint2 xg[4];  // four rows' loads in flight together
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) xg[i] = r0 + i < m ? load_x4(p, r0 + i, col) : make_uint2(0u, 0u);
+                        for (int i = 0; i < 4; ++i) xg[i] = r0 + i < m ? load_x4(p, r0 + i, col) : make_uint2(0u, 0u);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int row = r0 + i;
-                        if (row >= m) break;
-                        uint2 xr = xg[i];
-                        if (p.norm_w) {  // RMSNorm: fp16(fp16(x * s) * w), as exl3b_rmsnorm
-                            const float sc = inv_rms[row];
-                            const float2 a = __half22float2(u32_as_h2(xr.x)), b = __half22float2(u32_as_h2(xr.y));
-                            xr.x = h2_as_u32(__hmul2(__floats2half2_rn(a.x * sc, a.y * sc), u32_as_h2(nw.x)));
-                            xr.y = h2_as_u32(__hmul2(__floats2half2_rn(b.x * sc, b.y * sc), u32_as_h2(nw.y)));
-                        }
-                        const __half2 p01 = __hmul2(u32_as_h2(xr.x), u32_as_h2(sr.x));
-                        const __half2 p23 = __hmul2(u32_as_h2(xr.y), u32_as_h2(sr.y));
-                        float v[4] = {__low2float(p01), __high2float(p01), __low2float(p23), __high2float(p23)};
-                        had128_warp(v);
-                        if (mine) {
-                            dst[row * 8] = h2_as_u32(__floats2half2_rn(v[0] * kRScale, v[1] * kRScale));
-                            dst[row * 8 + 2] = h2_as_u32(__floats2half2_rn(v[2] * kRScale, v[3] * kRScale));
+                        for (int i = 0; i < 4; ++i) {
+                            if (r0 + i >= m) break;
+                            one_row(r0 + i, xg[i]);
                         }
                     }
                 }
