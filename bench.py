@@ -8,9 +8,11 @@ gate, up as one 2-group call; down) at M rows.  Steps rotate over layer copies w
 is far above the 126 MB L2, so every step streams its weights from HBM.  value = algorithmic
 bytes (packed codes + suh + svh + x + y) / device time, summed over all ranks' shards.
 
-N > 1: tensor parallel over N ranks (one process per GPU, NCCL): q/k/v/gate/up column-parallel
-(n sharded in 128-column blocks), o/down row-parallel (k sharded) followed by an NCCL all-reduce
-of the fp16 output, as vLLM's RowParallelLinear does.  Total work is fixed: scaling "strong".
+N > 1: tensor parallel over N ranks (one process per GPU, NCCL for the plumbing): q/k/v/gate/up
+column-parallel (n sharded in 128-column blocks), o/down row-parallel (k sharded) with the
+cross-rank sum inside the GEMV over peer memory (--tp-reduce nccl: an NCCL all-reduce of the fp16
+output after it, as vLLM's RowParallelLinear does).  Total work is fixed: scaling "strong".
+The `decode` key holds whole-model decode tok/s (exl3rocm.synthetic) at the same GPU count.
 
 --impl reference: times the CPU restatement of the reference's oracle (the reference path has no
 GPU implementation that runs here; its kernels are HIP/gfx1201) on the host cores, on a bounded
@@ -346,6 +348,8 @@ def bench_decode(torch, dev, steps: int, warmup: int, ctx: int = 32768,
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(st):
+            if world > 1:
+                graph.replay()  # untimed: its exchanges line the ranks' streams up
             e0.record(st)
             for _ in range(steps):
                 graph.replay()
@@ -356,6 +360,8 @@ def bench_decode(torch, dev, steps: int, warmup: int, ctx: int = 32768,
         t_host = torch.randint(0, shape.vocab, (dec.M,), dtype=torch.int64).pin_memory()
         o_host = torch.empty(dec.M, dtype=torch.int64).pin_memory()
         with torch.cuda.stream(st):
+            if world > 1:
+                graph.replay()
             e0.record(st)
             for _ in range(steps):
                 tokens.copy_(t_host, non_blocking=True)
@@ -508,6 +514,10 @@ def main():
     with ClockSampler(local) as clk, torch.cuda.stream(stream):
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            # one more untimed warm-up step: its in-kernel exchange lines the ranks' streams up, so
+            # the host-side skew of leaving the barrier stays out of the timed region
+            graphs[args.steps % copies].replay()
         t_start.record(stream)
         for i in range(args.steps):
             ev[i][0].record(stream)
@@ -559,6 +569,8 @@ def main():
     torch.cuda.synchronize()
     e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        if world > 1:
+            graphs[0].replay()  # untimed: its exchanges line the ranks' streams up
         e_s.record(stream)
         for i in range(args.steps):
             x.copy_(x_host, non_blocking=True)
