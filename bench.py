@@ -596,8 +596,13 @@ def main():
     if not args.no_extra and not args.no_decode and (world == 1 or comm is not None):
         del layers, outs, inputs
         torch.cuda.empty_cache()
-        extra["decode"] = bench_decode(torch, dev, steps=max(10, args.steps), warmup=args.warmup, world=world,
-                                       rank=rank, comm=comm, pg=pg)
+        try:
+            extra["decode"] = bench_decode(torch, dev, steps=max(10, args.steps), warmup=args.warmup, world=world,
+                                           rank=rank, comm=comm, pg=pg)
+        except Exception as e:  # a shape or setup error is the same on every rank: keep the layer line
+            extra["decode"] = {"error": repr(e)[:300]}
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
