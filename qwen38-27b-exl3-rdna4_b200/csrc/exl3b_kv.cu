@@ -310,6 +310,7 @@ struct KvAttnArgs {
     float* partial;              // [T][Hq][splits][kPartialStride]: acc, m, l
     // int4 exact rows
     const __half* exact_k; const __half* exact_v; const int32_t* exact_tag; const int32_t* seq_slots;
+    int tsplit;                  // > 1: that many warps share the split's keys (one warp holds all rows)
 };
 
 // int8 word (4 signed bytes) -> two half2 (bytes 0,1) and (bytes 2,3), exact
@@ -403,7 +404,7 @@ EXL3B_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_pe
 // reads 16 contiguous bytes (int8) or 8 (int4) of each of its 4 tokens per 16-token chunk.
 // Each warp owns 8 * NT query rows; the CTA's warps share nothing and never wait on one another.
 template <int KV, int NT>
-__global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
+__global__ void __launch_bounds__(32 * 4) kv_attn_kernel(const KvAttnArgs a) {
     griddep_launch();  // the split combine may be scheduled now; it waits for this grid's partials
     using Tr = KvTraits<KV>;
     using SM = AttnSmem<KV>;
@@ -421,9 +422,13 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     const int per = ((L + a.num_splits - 1) / a.num_splits + 31) & ~31;  // tokens per split, x32
     const int t_lo = split * per, t_hi = min(L, t_lo + per);
     if (t_lo >= t_hi) return;  // empty split: the reduce kernel skips it
-    // row r of the sequence = query (r / G), head kvh*G + r % G; this warp owns rows rbase + 0 .. 8NT-1
-    const int rbase = 8 * NT * warp;
-    if (rbase >= rows) return;  // no CTA-wide barrier below: warps run independently
+    // row r of the sequence = query (r / G), head kvh*G + r % G; this warp owns rows rbase + 0 .. 8NT-1.
+    // With tsplit > 1 every warp owns all rows (rows <= 8 NT) and takes every tsplit-th tile of the
+    // split; the warps' results are merged at the end (the only CTA-wide barrier).  Otherwise warps
+    // split the rows and run independently.
+    const int ts = a.tsplit;
+    const int rbase = ts > 1 ? 0 : 8 * NT * warp;
+    if (rbase >= rows) return;
 
     uint8_t* wsm = smem_raw + warp * SM::kWarpBytes;
     const uint32_t wsm_u = smem_u32(wsm);
@@ -465,9 +470,12 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
     // ---- tile loader: all of a 32-token tile's rows and scales, one cp.async group ----
     // Row r of a tile is stored with its 16-byte chunks XOR-swizzled by (r & (C16 - 1)), so that
     // the lanes reading the same chunk index of different rows hit different banks.
-    const int ntiles = (t_hi - t_lo + 31) >> 5;
+    const int ntiles_all = (t_hi - t_lo + 31) >> 5;
+    const int tw = ts > 1 ? warp : 0;  // this warp's first tile; its j-th is tw + j * tstep
+    const int tstep = ts > 1 ? ts : 1;
+    const int ntiles = ntiles_all > tw ? (ntiles_all - tw + tstep - 1) / tstep : 0;
     auto issue_tile = [&](int ti) {
-        const int t0 = t_lo + 32 * ti;
+        const int t0 = t_lo + 32 * (tw + ti * tstep);
         // block-id window: refill when the tile leaves it (the window is private to this warp)
         const int b_first = t0 >> lg, b_last = min(t0 + 31, t_hi - 1) >> lg;
         if (win_base < 0 || b_first < win_base || b_last >= win_base + SM::kBtWindow) {
@@ -546,7 +554,7 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
         else cp_async_commit();  // keep the group count in step
         cp_async_wait<SM::kRing - 1>();
         __syncwarp();
-        const int t0 = t_lo + 32 * ti;
+        const int t0 = t_lo + 32 * (tw + ti * tstep);
         const uint8_t* tile = wsm + (ti % SM::kRing) * SM::kTile;
         const float* ksc_s = reinterpret_cast<const float*>(tile + 2 * SM::kRows);
         const float* vsc_s = ksc_s + 32;
@@ -833,6 +841,60 @@ __global__ void __launch_bounds__(64) kv_attn_kernel(const KvAttnArgs a) {
             l_i[nt][h] = l;
         }
 
+    if (ts > 1) {
+        // merge the warps' (m, l, acc) of the same rows: each warp parks its values in its own ring
+        // area (field-major, conflict-free), then warp 0 combines them with weights 2^(m_w - M)
+        constexpr int kF = NT * 36;  // acc 32 + m 2 + l 2 per n-tile
+        static_assert(kF * 32 * 4 <= AttnSmem<KV>::kWarpBytes, "merge area");
+        float* park = reinterpret_cast<float*>(wsm);
+        __syncwarp();
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) park[(nt * 36 + 4 * j + e) * 32 + lane] = acc[nt][j][e];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                park[(nt * 36 + 32 + h) * 32 + lane] = m_i[nt][h];
+                park[(nt * 36 + 34 + h) * 32 + lane] = l_i[nt][h];
+            }
+        }
+        __syncthreads();
+        if (warp != 0) return;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float M = -INFINITY;
+                for (int w = 0; w < ts; ++w) {
+                    const float* pw = reinterpret_cast<const float*>(smem_raw + w * SM::kWarpBytes);
+                    M = fmaxf(M, pw[(nt * 36 + 32 + h) * 32 + lane]);
+                }
+                float l = 0.f, A[8][2];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) A[j][0] = A[j][1] = 0.f;
+                for (int w = 0; w < ts; ++w) {  // fixed warp order: deterministic
+                    const float* pw = reinterpret_cast<const float*>(smem_raw + w * SM::kWarpBytes);
+                    const float mw = pw[(nt * 36 + 32 + h) * 32 + lane];
+                    const float f = (mw == -INFINITY) ? 0.f : ex2(mw - M);
+                    l = fmaf(f, pw[(nt * 36 + 34 + h) * 32 + lane], l);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        A[j][0] = fmaf(f, pw[(nt * 36 + 4 * j + h) * 32 + lane], A[j][0]);
+                        A[j][1] = fmaf(f, pw[(nt * 36 + 4 * j + 2 + h) * 32 + lane], A[j][1]);
+                    }
+                }
+                m_i[nt][h] = M;
+                l_i[nt][h] = l;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    acc[nt][j][h] = A[j][0];
+                    acc[nt][j][2 + h] = A[j][1];
+                }
+            }
+    }
+
     // ---- partial of this split: acc (d order restored), m, l ----
     // acc[nt][j][h] is (d = 16g + 2j, row 2q + h), acc[nt][j][2 + h] is (d = 16g + 2j + 1, row 2q + h)
 #pragma unroll
@@ -1028,16 +1090,20 @@ static int kv_num_sms() {
 // run as a second, almost empty wave).  A split must stream enough keys to pay for its start-up:
 // 128 for up to 8 query rows per KV head (decode), 256 above (speculative verify).  rows = 1
 // gives the most splits any call of the shape can take (the workspace bound).
-static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len, int rows) {
-    const int want = (12 * kv_num_sms()) / (num_seqs * num_kv_heads);
-    const int min_keys = rows <= 8 ? 128 : 256;
+static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len, int rows, int ts = 1) {
+    const int want = (12 * kv_num_sms()) / (num_seqs * num_kv_heads * ts);
+    const int min_keys = (rows <= 8 ? 128 : 256) * ts;  // per warp: ts warps share a split
     const int by_len = (max_seq_len + min_keys - 1) / min_keys;
     return std::max(1, std::min(kMaxSplits, std::min(want, by_len)));
 }
 
+constexpr int kDecodeTsplit = 4;  // warps sharing a split's keys when one warp holds all query rows
+constexpr int kMaxAttnWarps = 4;  // the widest launch (the kernel's launch bound is 32 * 4)
+static_assert(kDecodeTsplit <= kMaxAttnWarps, "launch bound");
+
 template <int KV, int NT>
 static cudaError_t launch_attn(dim3 grid, int warps, const KvAttnArgs& a, cudaStream_t st) {
-    const int smem = 2 * AttnSmem<KV>::kWarpBytes;  // sized for the largest launch (2 warps)
+    const int smem = kMaxAttnWarps * AttnSmem<KV>::kWarpBytes;  // sized for the largest launch
     static std::once_flag once[64];
     static cudaError_t attr_err[64];
     int dev = 0;
@@ -1173,7 +1239,12 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     if (ws_bytes < exl3b_kv_attn_workspace_bytes(num_tokens, num_q_heads, num_seqs, num_kv_heads, max_seq_len))
         return EXL3B_WORKSPACE;
     cudaStream_t st = (cudaStream_t)stream;
-    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len), max_q_len * G);
+    // int4 decode over few (sequence, KV head) pairs (one warp holds all of a pair's query rows):
+    // kDecodeTsplit warps share each split's keys, so a split is that many times longer and the
+    // combine has as many times fewer partials (measured: int4 64k x 1 72.7 -> 58.2 us; int8 and
+    // batched decode measured the same or slower, so they keep one warp per split)
+    const int ts = (kv == 4 && max_q_len * G <= 8 && num_seqs * num_kv_heads <= 16) ? kDecodeTsplit : 1;
+    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len), max_q_len * G, ts);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const size_t qr_bytes = ((size_t)num_tokens * num_q_heads * kHD * 2 + 255) / 256 * 256;
     const __half* qin = reinterpret_cast<const __half*>(q);
@@ -1196,7 +1267,8 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     // query rows per (sequence, KV head): up to 24 in one warp (8 per n-tile), 32 in two warps of 16
     const int rows = max_q_len * G;
     const int nt = rows <= 8 ? 1 : rows <= 16 ? 2 : rows <= 24 ? 3 : 2;
-    const int warps = rows <= 24 ? 1 : 2;
+    const int warps = ts > 1 ? ts : rows <= 24 ? 1 : 2;
+    a.tsplit = ts;
     cudaError_t e;
     if (kv == 8)
         e = nt == 1 ? launch_attn<8, 1>(grid, warps, a, st) : nt == 2 ? launch_attn<8, 2>(grid, warps, a, st)
