@@ -135,9 +135,9 @@ EXL3B_DEV SbInfo sb_info(const GemvGroups& gg, int groups, int sb) {
 // Shared memory: a ring of kStages stages (R trellis rows of up to 64 tiles at a fixed stride,
 // then the unit's A_had rows), the fp32 accumulator tile [8 MT rows][kAccCols] where the decode
 // warps pool a finished super-block, and the mbarriers.
-template <int K, int MT>
+template <int K, int MT, int R0_>
 struct GemvSmem {
-    static constexpr int R0 = rows_per_unit(K);           // stage slots of 64 tiles
+    static constexpr int R0 = R0_;                         // stage slots of 64 tiles
     static constexpr int kTile = 32 * K;                  // bytes of one 16x16 tile
     static constexpr int kRowBytes = kSbTiles * kTile;    // stride of the stage slots
     static constexpr int kTrellisStage = R0 * kRowBytes;
@@ -378,9 +378,9 @@ EXL3B_DEV void norm_partials(const GemvParams& p, float* part, int warp, int lan
     }
 }
 
-template <int K, int CB, int MT>
+template <int K, int CB, int MT, int R0_>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
-    using S = GemvSmem<K, MT>;
+    using S = GemvSmem<K, MT, R0_>;
     constexpr int kStages = S::kStages;
     constexpr int R0 = S::R0;
     const int q = p.q, R = R0 * p.q;  // k-rows per unit; row r sits in slot r / q at tile (r % q) * 64 / q
@@ -743,18 +743,20 @@ static void split_super_blocks(int blocks, int maxb, int& count, int& base, int&
 }
 
 struct Partition {
-    int q, ku, units, ctas, sb_cols, super_blocks;
+    int r0, q, ku, units, ctas, sb_cols, super_blocks;
 };
 
 // The widest super-blocks (smallest q) that still give every column block at most about eight
 // CTAs to reduce over: narrow layers (o, down, k/v) get 256- or 512-column super-blocks with more
 // k-rows per unit, so that their cross-CTA sums stay short.  Depends on the shape and K only.
-static Partition partition(int k, int K, int groups, const int* n) {
-    const int kt = k / 16, r0 = rows_per_unit(K);
+static Partition partition(int k, int K, int groups, const int* n, int r0) {
+    const int kt = k / 16;
     Partition q = {};
+    q.r0 = r0;
     for (int qq : {1, 2, 4}) {
         if (kt % (r0 * qq) || r0 * qq > kMaxUnitRows) break;  // rows per unit must divide k / 16
         Partition t = {};
+        t.r0 = r0;
         t.q = qq;
         t.ku = kt / (r0 * qq);
         int widest = 0;
@@ -773,6 +775,22 @@ static Partition partition(int k, int K, int groups, const int* n) {
     return q;
 }
 
+// Rows per unit slot: 8 (fewer unit hand-offs) at K <= 4 unless units of 2 balance the CTAs clearly
+// better (small layers and tensor-parallel shards, whose few large units would leave SMs idle: an
+// o shard at TP 8 has 25 units of 8 rows for 148 SMs).  Cost: the busiest CTA's units x (their
+// k-rows + half a row of hand-off); units of 2 must cost under 0.8x, since a marginal gain measured
+// as a loss inside a chain of launches (the full o at M = 1: 26.5 us alone with units of 2 against
+// 27.5, but its layer step 122.2 against 119.6 us).  Depends on the shape and K only, never on m.
+static Partition choose_partition(int k, int K, int groups, const int* n) {
+    const Partition a = partition(k, K, groups, n, rows_per_unit(K));
+    if (rows_per_unit(K) == 2) return a;
+    const Partition b = partition(k, K, groups, n, 2);
+    auto cost = [](const Partition& t) {
+        return (double)((t.units + t.ctas - 1) / std::max(t.ctas, 1)) * (t.r0 + 0.5);
+    };
+    return cost(b) < 0.8 * cost(a) ? b : a;
+}
+
 struct WsLayout {
     size_t counters, partials, stage, total;
 };
@@ -787,10 +805,10 @@ static WsLayout ws_layout(int m, int k, int groups, const Partition& q, int64_t 
     return L;
 }
 
-template <int K, int CB, int MT>
+template <int K, int CB, int MT, int R0>
 static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st) {
-    using S = GemvSmem<K, MT>;
-    auto kern = gemv_kernel<K, CB, MT>;
+    using S = GemvSmem<K, MT, R0>;
+    auto kern = gemv_kernel<K, CB, MT, R0>;
     static std::once_flag once[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -813,16 +831,17 @@ static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st) {
 }
 
 template <int CB, int MT>
-static cudaError_t launch_gemv_k(int K, const GemvParams& p, cudaStream_t st) {
+static cudaError_t launch_gemv_k(int K, int r0, const GemvParams& p, cudaStream_t st) {
+    const bool r2 = r0 == 2;  // K <= 4 has units of 8 or 2 rows per slot, K > 4 of 2
     switch (K) {
-        case 1: return launch_gemv<1, CB, MT>(p, st);
-        case 2: return launch_gemv<2, CB, MT>(p, st);
-        case 3: return launch_gemv<3, CB, MT>(p, st);
-        case 4: return launch_gemv<4, CB, MT>(p, st);
-        case 5: return launch_gemv<5, CB, MT>(p, st);
-        case 6: return launch_gemv<6, CB, MT>(p, st);
-        case 7: return launch_gemv<7, CB, MT>(p, st);
-        default: return launch_gemv<8, CB, MT>(p, st);
+        case 1: return r2 ? launch_gemv<1, CB, MT, 2>(p, st) : launch_gemv<1, CB, MT, 8>(p, st);
+        case 2: return r2 ? launch_gemv<2, CB, MT, 2>(p, st) : launch_gemv<2, CB, MT, 8>(p, st);
+        case 3: return r2 ? launch_gemv<3, CB, MT, 2>(p, st) : launch_gemv<3, CB, MT, 8>(p, st);
+        case 4: return r2 ? launch_gemv<4, CB, MT, 2>(p, st) : launch_gemv<4, CB, MT, 8>(p, st);
+        case 5: return launch_gemv<5, CB, MT, 2>(p, st);
+        case 6: return launch_gemv<6, CB, MT, 2>(p, st);
+        case 7: return launch_gemv<7, CB, MT, 2>(p, st);
+        default: return launch_gemv<8, CB, MT, 2>(p, st);
     }
 }
 
@@ -861,7 +880,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
         for (int r = 0; r < comm->tp_size; ++r)
             if (!comm->buffers[r] || !aligned(comm->buffers[r], 256)) return EXL3B_BAD_ARG;
     }
-    const Partition q = partition(k, K, groups, n);
+    const Partition q = choose_partition(k, K, groups, n);
     const WsLayout L = ws_layout(m, k, groups, q, act ? n_total : 0);
     if (ws_bytes < L.total) return EXL3B_WORKSPACE;
 
@@ -919,9 +938,9 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     cudaError_t e;
     const bool mt2 = m > 8;
     switch (codebook) {
-        case 0: e = mt2 ? launch_gemv_k<0, 2>(K, p, st) : launch_gemv_k<0, 1>(K, p, st); break;
-        case 1: e = mt2 ? launch_gemv_k<1, 2>(K, p, st) : launch_gemv_k<1, 1>(K, p, st); break;
-        default: e = mt2 ? launch_gemv_k<2, 2>(K, p, st) : launch_gemv_k<2, 1>(K, p, st); break;
+        case 0: e = mt2 ? launch_gemv_k<0, 2>(K, q.r0, p, st) : launch_gemv_k<0, 1>(K, q.r0, p, st); break;
+        case 1: e = mt2 ? launch_gemv_k<1, 2>(K, q.r0, p, st) : launch_gemv_k<1, 1>(K, q.r0, p, st); break;
+        default: e = mt2 ? launch_gemv_k<2, 2>(K, q.r0, p, st) : launch_gemv_k<2, 1>(K, q.r0, p, st); break;
     }
     return cuda_status(e);
 }
