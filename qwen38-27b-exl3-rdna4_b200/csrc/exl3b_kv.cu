@@ -126,6 +126,10 @@ EXL3B_DEV void rope4(float (&x)[4], const float* cs, int lane) {
 }
 
 __global__ void kv_int8_write_rope_kernel(const KvWriteArgs a, const KvRopeArgs r) {
+    // a programmatic dependent launch: the attention after it may be scheduled now; qkv comes from
+    // the previous kernel
+    griddep_launch();
+    griddep_wait();
     const int slots = r.nq + a.num_heads;
     const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (item >= (int64_t)a.num_tokens * slots) return;
@@ -406,6 +410,7 @@ EXL3B_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_pe
 template <int KV, int NT>
 __global__ void __launch_bounds__(32 * 4) kv_attn_kernel(const KvAttnArgs a) {
     griddep_launch();  // the split combine may be scheduled now; it waits for this grid's partials
+    griddep_wait();    // a programmatic dependent launch: q and the cache rows come from earlier kernels
     using Tr = KvTraits<KV>;
     using SM = AttnSmem<KV>;
     constexpr int RB = SM::kRowBytes;
@@ -1112,8 +1117,17 @@ static cudaError_t launch_attn(dim3 grid, int warps, const KvAttnArgs& a, cudaSt
         attr_err[dev & 63] = cudaFuncSetAttribute(kv_attn_kernel<KV, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     });
     if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
-    kv_attn_kernel<KV, NT><<<grid, 32 * warps, warps * AttnSmem<KV>::kWarpBytes, st>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(32 * warps);
+    cfg.dynamicSmemBytes = warps * AttnSmem<KV>::kWarpBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kv_attn_kernel<KV, NT>, a);
 }
 
 static bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
@@ -1180,8 +1194,16 @@ extern "C" int exl3b_kv_int8_write_rope(const uint16_t* qkv, int64_t ld, uint16_
     r.q_out = reinterpret_cast<__half*>(q_out); r.ld_q = ld_q; r.nq = num_q_heads;
     r.positions = positions; r.cos_sin = cos_sin; r.max_pos = max_position;
     const int64_t items = num_tokens * (num_q_heads + num_kv_heads);
-    kv_int8_write_rope_kernel<<<(unsigned)((items + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a, r);
-    return cuda_status(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((items + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kv_int8_write_rope_kernel, a, r));
 }
 
 extern "C" int exl3b_kv_int4_write(const void* key, const void* value, int dtype, int64_t num_tokens,
