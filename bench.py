@@ -44,6 +44,20 @@ LAYER = [("q", HIDDEN, HEADS * HEAD_DIM, False), ("k", HIDDEN, KV_HEADS * HEAD_D
 MODULES = [("qkv", ["q", "k", "v"]), ("o", ["o"]), ("gate_up", ["gate", "up"]), ("down", ["down"])]
 L2_BYTES = 126 * 1024 * 1024
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gemv_kernel launch of the gate_up
+# call at K = 4, m = 1 on one GPU, from one ncu capture.  A capture describes the kernel source it was
+# taken from: the figure is reported only while the GEMV sources hash to src_sha256, else null.
+GEMV_TRAFFIC = {"src_sha256": "", "bytes": None}
+
+
+def gemv_source_sha() -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for f in ("exl3b_gemv.cu", "exl3b_common.cuh"):
+        with open(os.path.join(ROOT, "qwen38-27b-exl3-rdna4_b200", "csrc", f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()
+
 
 def linear_bytes(k: int, n: int, K: int, m: int) -> int:
     """Algorithmic bytes of one EXL3 linear: codes + suh + svh + x + y (fp16)."""
@@ -181,6 +195,8 @@ def layer_bytes(K, m, tp):
 # CPU baseline: the oracle restatement on the host cores (bounded sample)
 # ---------------------------------------------------------------------------------------------
 def _cpu_slice(args):
+    """One worker's share: generate its column slice (untimed), then time the oracle linear on it.
+    Returns (start, end) of the timed call on the host's monotonic clock."""
     k, n_cols, K, seed = args
     from oracle import exl3_oracle as O
     rng = np.random.default_rng(seed)
@@ -190,32 +206,41 @@ def _cpu_slice(args):
     x = rng.standard_normal((1, k)).astype(np.float16)
     t0 = time.perf_counter()
     O.linear(x, tr, K, suh, svh, 2)
-    return time.perf_counter() - t0
+    return t0, time.perf_counter()
+
+
+def _cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def cpu_baseline(K: int, budget_cols: int = 524288) -> dict:
     """Time the oracle's linear (M=1, mul1) on a column sample of gate_proj-shaped weights (k = 5120),
     one slice per host core in a spawn pool, about ten seconds of host work in all; report the
-    metric's unit for that sample."""
+    metric's unit for that sample.  Only the oracle calls are timed: the span from the first worker's
+    start to the last worker's end (pool start-up and code generation excluded)."""
     import multiprocessing as mp
     cores = os.cpu_count() or 1
     per = max(128, (budget_cols // cores) // 128 * 128)
     jobs = [(HIDDEN, per, K, 1000 + i) for i in range(cores)]
     ctx = mp.get_context("spawn")
-    t0 = time.perf_counter()
     with ctx.Pool(cores) as pool:
-        pool.map(_cpu_slice, jobs)
-    wall = time.perf_counter() - t0
-    # generation of the synthetic codes is inside the slices but outside each slice's timer;
-    # the reported value uses the wall time of the whole pool (generation included: conservative)
+        spans = pool.map(_cpu_slice, jobs)
+    compute = max(e for _, e in spans) - min(s for s, _ in spans)
     nbytes = sum(linear_bytes(HIDDEN, per, K, 1) for _ in jobs)
-    return {"value": nbytes / wall / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+    return {"value": nbytes / compute / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "cpu_model": _cpu_model(),
             "sample": f"oracle linear M=1 mul1 K={K}: {cores} x (5120 x {per}) column slices of gate_proj, "
-                      f"process pool, {wall:.1f} s wall"}
+                      f"process pool, {compute:.1f} s of oracle calls (first start to last end)"}
 
 
 # ---------------------------------------------------------------------------------------------
-# paged KV attention (BASELINE config 3) and prefill (M = 2048)
+# paged KV attention (40 q / 8 kv heads, contexts 4k-64k) and prefill (M = 2048)
 # ---------------------------------------------------------------------------------------------
 KV_HQ, KV_HKV, KV_D, KV_BS = 40, 8, 128, 16
 
@@ -224,7 +249,7 @@ def _flush_l2(torch, buf):
     buf.add_(1)  # a write larger than L2 between timed calls
 
 
-def bench_kv(torch, dev, kind: int, ctx: int, batch: int, q_len: int, iters: int = 5) -> dict:
+def bench_kv(torch, dev, kind: int, ctx: int, batch: int, q_len: int, iters: int = 20) -> dict:
     """Decode (q_len 1) or verify attention over an int8 / int4 cache of `batch` sequences of `ctx`
     tokens, 40 q heads / 8 kv heads, head 128, block 16.  K/V are written through the write kernel
     from N(0,1) rows with 1 % of channels x8.  GB/s counts the cache bytes the call must read."""
@@ -558,9 +583,8 @@ def main():
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = gu_bytes / (gu_ms_med * 1e-3) / 1e9
-    # DRAM bytes (read + write) of one gemv_kernel launch of this call, from the ncu capture
-    # summarised in profiles/gemv_kernel_gate_up_m1_k4.md (measured for K = 4, m = 1 only)
-    traffic = (89.314304e6 + 3.256320e6) if (K == 4 and M == 1 and world == 1) else None
+    traffic = GEMV_TRAFFIC["bytes"] if (K == 4 and M == 1 and world == 1 and
+                                         gemv_source_sha() == GEMV_TRAFFIC["src_sha256"]) else None
 
     # ---- end to end: pinned host x -> device, the layer's ops (graph), y -> pinned host ----
     x_host = torch.randn((M, HIDDEN), dtype=torch.float32).to(torch.bfloat16).pin_memory()
@@ -626,7 +650,8 @@ def main():
                      "kernel": "gate_up linear_groups call (gemv_kernel, graph-replayed), median "
                                f"of {n_calls} event-timed calls, {gu_bytes} algorithmic bytes per call",
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel "
-                                       "launch (profiles/gemv_kernel_gate_up_m1_k4.md)" if traffic else None,
+                                       "launch of this call, captured from the current GEMV source" if traffic
+                                       else "null: no ncu capture of the current GEMV source",
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650"},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 2),

@@ -192,8 +192,10 @@ EXL3B_API int exl3b_kv_int8_attn(const uint16_t* q, uint16_t* out, int num_token
 
 /* The same over the int4 cache: q is rotated with the RHT, rows with a matching exact tag (first 4
  * and newest 128 positions of a request slot) are read from the exact fp16 rows, and the output is
- * rotated back: out = H(rot) * signs / 128.  Replaces the reference's kv_int4.attention
- * (vllm_plugin/exl3rocm/kv_int4.py:345-563). */
+ * rotated back: out = fp16(H(rot) * signs / 128 + out_bias[kv head of the query head]).  out_bias
+ * (optional, fp32 [num_kv_heads][128]) is the value mean of a cache written with bias_v = -(mean_v @
+ * diag(signs) H) (the centering of kv_int4.py:120-158, added back as :563 does).  Replaces the
+ * reference's kv_int4.attention (vllm_plugin/exl3rocm/kv_int4.py:345-563). */
 EXL3B_API int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_tokens, int num_q_heads,
                                  int num_kv_heads, int head_size, const uint8_t* key_cache,
                                  const uint8_t* value_cache, const float* k_scale, const float* v_scale,
@@ -201,7 +203,8 @@ EXL3B_API int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_token
                                  const int32_t* seq_lens, const int32_t* query_start_loc, int num_seqs,
                                  int max_q_len, int max_seq_len, float softmax_scale, const float* rht_signs,
                                  const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
-                                 const int32_t* seq_slots, void* workspace, size_t workspace_bytes, void* stream);
+                                 const int32_t* seq_slots, const float* out_bias, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* Prefill over the quantised caches: gather the blocks listed in block_ids (n entries) and dequantise
  * them to fp16 rows out[n][block_size][num_kv_heads][128], for an fp16 attention kernel to read.
@@ -225,19 +228,27 @@ EXL3B_API int exl3b_kv_int4_gather(const uint8_t* cache, const float* scale, int
  * no counterpart in the reference: the reference always receives its scratch from the torch
  * caching allocator.
  * Same arguments, results and limits as exl3b_linear (each row bitwise equal to exl3b_linear's),
- * but the scratch lives in one static device array of EXL3B_NOALLOC_SCRATCH_BYTES (8 MiB) that
- * every GPU loading this library holds until exit; the call allocates nothing.  Calls whose
- * workspace (exl3b_linear_workspace_bytes(m, k, 1, n)) exceeds it return EXL3B_TOO_LARGE
- * before launching anything (m <= 16 with k <= 65536 always fits on a B200).
- * The first call on a device resolves the array's device address with that device current
- * (a one-time, synchronous set-up): make it before any stream capture.  Every call clears the
- * array's counter region on `stream` first, and all calls share the array, so calls that can
- * overlap on the GPU (different streams, or graphs replayed concurrently) race: issue them in
- * one stream order. */
-#define EXL3B_NOALLOC_SCRATCH_BYTES (8u << 20)
+ * but the scratch lives in one static device array of EXL3B_NOALLOC_SCRATCH_BYTES (32 MiB) that
+ * every GPU loading this library holds until exit; the call allocates nothing.  A call whose
+ * scratch need exceeds the array returns EXL3B_TOO_LARGE before launching anything.  The need is
+ * at most 33280 + 4 * m * (1024 * SMs + 2 * n) bytes, so on a B200 (148 SMs) every call with
+ * m <= 16 and n <= 131072 fits, at any k, K and codebook (m = 16 at n = 17408 needs 10.8 MB).
+ * The first call on a device resolves the array's device address with that device current (a
+ * one-time set-up; if it fails, the next call tries again): make it before any stream capture — a
+ * first call on a stream that is being captured returns EXL3B_BAD_ARG without touching the stream.
+ * Every call clears the array's counter region and error word on `stream` first, and all calls
+ * share the array, so calls that can overlap on the GPU (different streams, or graphs replayed
+ * concurrently) race: issue them in one stream order. */
+#define EXL3B_NOALLOC_SCRATCH_BYTES (32u << 20)
 EXL3B_API int exl3b_linear_noalloc(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K,
                                    int codebook, const uint16_t* suh, const uint16_t* svh, uint16_t* y,
                                    int64_t ldy, void* stream);
+/* The kernel error word of the last exl3b_linear_noalloc call on the current device (0 = none;
+ * otherwise the code of a bounded wait that gave up, after which that call's y is not valid) into
+ * *out, synchronising `stream`.  Read it before the next call, which clears it.  No counterpart in
+ * the reference (the diagnostic of the static scratch, as exl3b_linear_workspace_error is of a
+ * caller's workspace). */
+EXL3B_API int exl3b_linear_noalloc_error(int* out, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Tensor-parallel row-parallel linear with the all-reduce fused into the kernel.  The reference

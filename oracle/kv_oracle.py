@@ -15,10 +15,14 @@ int4 per-token-head (reference vllm_plugin/exl3rocm/kv_int4.py):
   attention :345-563 (rotated q; S = q.(nibble - zp) * (softmax_scale / d) * k_scale; exact rows
             with scale 1; P * v_scale . (nibble - zp); output un-rotated by (H diag(s)) / d)
 
-Parity status: the int8 and int4 GPU kernels of the reference are Triton and cannot run here, and
-the int4 RHT sign vector comes from a vLLM 0.28 helper that is absent, so these restatements are
-unpinned against reference outputs; they are the checker for this repository's kernels (codes and
-scales bit-exact, attention within tolerance of a float64 softmax).
+Parity status: pinned.  tests/golden/make_kv_golden.py runs the reference's own Triton kernels
+(vLLM 0.22's int8 per-token-head write and unified attention; the reference's kv_int4.py write and
+attention, with and without centering) under Triton's CPU interpreter and commits their outputs;
+tests/test_kv_golden.py checks this module against them: int8 codes and scales bit-exact, int4 codes
+and exact rows bit-exact, int4 scales bit-exact except a last-place difference where the row mean
+is summed in another order, attention within the tolerance of a float64 softmax.  One input is not
+the reference's: the int4 RHT sign vector comes from a vLLM 0.28 helper absent here, so the
+fixtures use this repository's seeded vector (the format is parameterised by it).
 """
 from __future__ import annotations
 
@@ -238,15 +242,21 @@ def exact_index(pos: int) -> int:
 
 
 def int4_write(key, value, slot_mapping, positions, req_slots, key_cache, value_cache, k_scale, v_scale,
-               exact_k, exact_v, exact_tag, seq_lens_after, signs):
+               exact_k, exact_v, exact_tag, seq_lens_after, signs, bias_k=None, bias_v=None):
     """Rotate, quantise and pack K and V rows; keep exact fp16 rows for positions < SINKS and for the
     newest TAIL positions of each request (exact_* [slots, SINKS + TAIL, H, D], tag [slots, SINKS + TAIL]).
 
     positions[t], req_slots[t]: the token's position in its sequence and its request slot;
-    seq_lens_after[t]: that sequence's length once this batch is written."""
+    seq_lens_after[t]: that sequence's length once this batch is written.
+    bias_k / bias_v [H, D] float32 (optional): rotated-domain biases -(mean @ diag(s) H) added to the
+    rotated rows before quantisation, the centering of kv_int4.py:133-148, 265-266."""
     bs = key_cache.shape[1]
     yk = fwht128_f32(np.asarray(key, np.float32) * signs)
     yv = fwht128_f32(np.asarray(value, np.float32) * signs)
+    if bias_k is not None:
+        yk = (yk + np.asarray(bias_k, np.float32)[None]).astype(np.float32)
+    if bias_v is not None:
+        yv = (yv + np.asarray(bias_v, np.float32)[None]).astype(np.float32)
     ck, sk = int4_quantize_rows(yk)
     cv, sv = int4_quantize_rows(yv)
     for t, slot in enumerate(np.asarray(slot_mapping)):
@@ -264,10 +274,11 @@ def int4_write(key, value, slot_mapping, positions, req_slots, key_cache, value_
 
 
 def int4_attention(q, key_cache, value_cache, k_scale, v_scale, exact_k, exact_v, exact_tag, req_slot_of_seq,
-                   block_table, seq_lens, query_start_loc, softmax_scale, signs):
+                   block_table, seq_lens, query_start_loc, softmax_scale, signs, v_mean=None):
     """Attention over the int4 cache with exact-row substitution, computed in the rotated domain and
     un-rotated (the RHT is orthogonal up to the factor d, so this equals attention over the
-    dequantised, un-rotated rows)."""
+    dequantised, un-rotated rows).  v_mean [H_kv, D] (optional): the value mean of a centred cache,
+    added back to the output of every query head of that KV head (kv_int4.py:470-480, 563)."""
     d = q.shape[-1]
 
     def rows(cache, scale, ex, s, n):
@@ -283,4 +294,8 @@ def int4_attention(q, key_cache, value_cache, k_scale, v_scale, exact_k, exact_v
     rot = paged_attention(qr, seq_lens, query_start_loc, block_table, softmax_scale / d,
                           lambda s, n: rows(key_cache, k_scale, exact_k, s, n),
                           lambda s, n: rows(value_cache, v_scale, exact_v, s, n))
-    return rht_inverse_d(rot, signs)
+    out = rht_inverse_d(rot, signs)
+    if v_mean is not None:
+        vm = np.asarray(v_mean, np.float64)
+        out = out + np.repeat(vm, q.shape[1] // vm.shape[0], axis=0)[None]
+    return out

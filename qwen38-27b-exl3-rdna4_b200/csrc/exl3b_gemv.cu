@@ -805,6 +805,13 @@ static WsLayout ws_layout(int m, int k, int groups, const Partition& q, int64_t 
     return L;
 }
 
+// The workspace bytes a one-group call of this shape really uses (the partition its launch takes),
+// for callers whose scratch has a fixed size.  k, n multiples of 128, 1 <= K <= 8.
+size_t linear_workspace_exact(int m, int k, int n, int K) {
+    const int nn[1] = {n};
+    return ws_layout(m, k, 1, choose_partition(k, K, 1, nn), 0).total;
+}
+
 template <int K, int CB, int MT, int R0>
 static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st) {
     using S = GemvSmem<K, MT, R0>;

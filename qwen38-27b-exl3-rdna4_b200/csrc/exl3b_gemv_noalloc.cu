@@ -11,10 +11,11 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
                 int codebook, const uint16_t* const* suh, const uint16_t* const* svh, uint16_t* const* y,
                 int64_t ldy, void* workspace, size_t ws_bytes, void* stream, const exl3b_tp_comm* comm,
                 const uint16_t* norm_w, float norm_eps);
+size_t linear_workspace_exact(int m, int k, int n, int K);
 
 // The scratch: held by every device that loads the library, shared by all calls on that device.
-// In host code `g_noalloc_scratch` names a host-side stand-in, never the device memory; the
-// device address comes from cudaGetSymbolAddress below.
+// Static device memory starts zeroed.  In host code `g_noalloc_scratch` names a host-side stand-in,
+// never the device memory; the device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[EXL3B_NOALLOC_SCRATCH_BYTES];
 
 // Bytes at the start of a linear workspace that must be zero when a call starts (error word +
@@ -22,24 +23,29 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[EXL3B_NOALLOC_SCRATCH
 constexpr size_t kZeroBytes = EXL3B_WS_ZERO_BYTES;
 
 constexpr int kMaxDevices = 64;
-static std::once_flag g_setup_once[kMaxDevices];
-static void* g_scratch_ptr[kMaxDevices];
-static cudaError_t g_setup_err[kMaxDevices];
+static std::mutex g_setup_mu;
+static void* g_scratch_ptr[kMaxDevices];  // set once a device's set-up has succeeded
 
-// Once per device, with that device current: resolve the device address of the array and zero it.
-static int scratch_for_current_device(void** out) {
+// The array's device address on the current device.  The first call on a device resolves it with
+// that device current; a failed set-up is not remembered, so the next call tries again.
+static int scratch_for_current_device(void** out, cudaStream_t stream) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_status(e);
     if (dev < 0 || dev >= kMaxDevices) return EXL3B_BAD_ARG;
-    std::call_once(g_setup_once[dev], [dev] {
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    if (!g_scratch_ptr[dev]) {
+        // the set-up belongs before any capture: refuse it (without touching any stream) when the
+        // stream is being captured
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing(stream, &cap);
+        if (e != cudaSuccess) return cuda_status(e);
+        if (cap != cudaStreamCaptureStatusNone) return EXL3B_BAD_ARG;
         void* p = nullptr;
-        cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (err == cudaSuccess) err = cudaMemset(p, 0, kZeroBytes);
-        g_scratch_ptr[dev] = (err == cudaSuccess) ? p : nullptr;
-        g_setup_err[dev] = err;
-    });
-    if (g_setup_err[dev] != cudaSuccess) return cuda_status(g_setup_err[dev]);
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_status(e);
+        g_scratch_ptr[dev] = p;
+    }
     *out = g_scratch_ptr[dev];
     return EXL3B_OK;
 }
@@ -51,12 +57,12 @@ using namespace exl3b;
 extern "C" int exl3b_linear_noalloc(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K,
                                     int codebook, const uint16_t* suh, const uint16_t* svh, uint16_t* y,
                                     int64_t ldy, void* stream) {
-    if (m < 1 || m > EXL3B_GEMV_MAX_ROWS || k < 128 || n < 128) return EXL3B_DECLINED;
-    const size_t need = exl3b_linear_workspace_bytes(m, k, 1, n);
-    if (need == 0) return EXL3B_DECLINED;
-    if (need > EXL3B_NOALLOC_SCRATCH_BYTES) return EXL3B_TOO_LARGE;
+    if (m < 1 || m > EXL3B_GEMV_MAX_ROWS || k < 128 || n < 128 || k % 128 || n % 128 || K < 1 || K > 8)
+        return EXL3B_DECLINED;
+    // the exact bytes this call's partition uses, the same layout exl3b_linear checks
+    if (linear_workspace_exact(m, k, n, K) > EXL3B_NOALLOC_SCRATCH_BYTES) return EXL3B_TOO_LARGE;
     void* scratch = nullptr;
-    int st = scratch_for_current_device(&scratch);
+    int st = scratch_for_current_device(&scratch, (cudaStream_t)stream);
     if (st != EXL3B_OK) return st;
     // the counters and the error word must start at zero; a failed earlier call may have left
     // them otherwise, so clear them in stream order before this call's kernels
@@ -69,4 +75,12 @@ extern "C" int exl3b_linear_noalloc(const uint16_t* x, int m, int k, const uint1
     int nn[1] = {n};
     return linear_impl(x, m, k, 1, tr, nn, K, codebook, su, sv, yy, ldy, scratch, EXL3B_NOALLOC_SCRATCH_BYTES,
                        stream, nullptr, nullptr, 0.f);
+}
+
+extern "C" int exl3b_linear_noalloc_error(int* out, void* stream) {
+    if (!out) return EXL3B_BAD_ARG;
+    void* scratch = nullptr;
+    int st = scratch_for_current_device(&scratch, (cudaStream_t)stream);
+    if (st != EXL3B_OK) return st;
+    return exl3b_linear_workspace_error(scratch, out, stream);
 }

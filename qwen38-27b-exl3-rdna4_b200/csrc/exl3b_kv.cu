@@ -934,6 +934,8 @@ struct KvReduceArgs {
     const int32_t* seq_lens; const int32_t* query_start_loc;
     int num_seqs, num_tokens, num_q_heads, num_splits;
     const float* unrot_signs;  // int4: RHT signs, else null
+    const float* out_bias;     // int4, optional: value mean [kv heads][128] added to the un-rotated output
+    int group;                 // query heads per KV head
 };
 
 // One CTA per (query token, q head) of W = ceil(splits / 8) warps (at most 32).  The split maxima
@@ -1013,6 +1015,11 @@ __global__ void __launch_bounds__(32 * kReduceWarps) kv_reduce_kernel(const KvRe
         had128_warp(r);
 #pragma unroll
         for (int i = 0; i < 4; ++i) r[i] = r[i] * a.unrot_signs[4 * lane + i] * (1.f / kHD);
+        if (a.out_bias) {  // the centering's value mean, added before the one fp16 rounding (kv_int4.py:563)
+            const float* b = a.out_bias + (int64_t)((int)(item % a.num_q_heads) / a.group) * kHD + 4 * lane;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) r[i] = __fadd_rn(r[i], b[i]);
+        }
     }
     reinterpret_cast<uint2*>(a.out + item * kHD)[lane] =
         make_uint2(h2_as_u32(__floats2half2_rn(r[0], r[1])), h2_as_u32(__floats2half2_rn(r[2], r[3])));
@@ -1248,7 +1255,8 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
                           int64_t bt_stride, const int32_t* seq_lens, const int32_t* query_start_loc, int num_seqs,
                           int max_q_len, int max_seq_len, float softmax_scale, const float* rht_signs,
                           const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
-                          const int32_t* seq_slots, void* workspace, size_t ws_bytes, void* stream) {
+                          const int32_t* seq_slots, const float* out_bias, void* workspace, size_t ws_bytes,
+                          void* stream) {
     if (head_size != kHD || !pow2(block_size)) return EXL3B_DECLINED;
     if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return EXL3B_DECLINED;
     if (num_tokens == 0) return EXL3B_OK;
@@ -1303,6 +1311,7 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     r.partial = a.partial; r.out = reinterpret_cast<__half*>(out); r.seq_lens = seq_lens;
     r.query_start_loc = query_start_loc; r.num_seqs = num_seqs; r.num_tokens = num_tokens;
     r.num_q_heads = num_q_heads; r.num_splits = S; r.unrot_signs = kv == 4 ? rht_signs : nullptr;
+    r.out_bias = kv == 4 ? out_bias : nullptr; r.group = G;
     const int64_t items = (int64_t)num_tokens * num_q_heads;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)items);
@@ -1326,7 +1335,7 @@ extern "C" int exl3b_kv_int8_attn(const uint16_t* q, uint16_t* out, int num_toke
     return kv_attn_common(8, q, out, num_tokens, num_q_heads, num_kv_heads, head_size, key_cache, value_cache,
                           k_scale, v_scale, block_size, block_table, bt_stride, seq_lens, query_start_loc, num_seqs,
                           max_q_len, max_seq_len, softmax_scale, nullptr, nullptr, nullptr, nullptr, nullptr,
-                          workspace, workspace_bytes, stream);
+                          nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_tokens, int num_q_heads,
@@ -1336,11 +1345,12 @@ extern "C" int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_toke
                                   const int32_t* seq_lens, const int32_t* query_start_loc, int num_seqs,
                                   int max_q_len, int max_seq_len, float softmax_scale, const float* rht_signs,
                                   const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
-                                  const int32_t* seq_slots, void* workspace, size_t workspace_bytes, void* stream) {
+                                  const int32_t* seq_slots, const float* out_bias, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
     return kv_attn_common(4, q, out, num_tokens, num_q_heads, num_kv_heads, head_size, key_cache, value_cache,
                           k_scale, v_scale, block_size, block_table, bt_stride, seq_lens, query_start_loc, num_seqs,
                           max_q_len, max_seq_len, softmax_scale, rht_signs, exact_k, exact_v, exact_tag, seq_slots,
-                          workspace, workspace_bytes, stream);
+                          out_bias, workspace, workspace_bytes, stream);
 }
 
 static int kv_gather_common(int kv, const void* cache, const float* scale, int block_size, int num_kv_heads,

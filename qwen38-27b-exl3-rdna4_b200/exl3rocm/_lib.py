@@ -48,6 +48,7 @@ SIGNATURES = {
                                            ctypes.POINTER(c_vp), i64, c_vp, sz, c_vp]),
     "exl3b_linear_workspace_error": (i32, [c_vp, ctypes.POINTER(i32), c_vp]),
     "exl3b_linear_noalloc": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp]),
+    "exl3b_linear_noalloc_error": (i32, [ctypes.POINTER(i32), c_vp]),
     "exl3b_kv_int8_write": (i32, [c_vp, c_vp, i32, i64, i32, i32, i64, i64, i64, i64, c_vp, c_vp, c_vp, c_vp, c_vp,
                                   i32, c_vp]),
     "exl3b_kv_int8_write_rope": (i32, [c_vp, i64, c_vp, i64, i64, i32, i32, c_vp, c_vp, i64, c_vp, c_vp, c_vp, c_vp,
@@ -66,7 +67,7 @@ SIGNATURES = {
     "exl3b_kv_int8_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,
                                  i32, i32, i32, f32, c_vp, sz, c_vp]),
     "exl3b_kv_int4_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,
-                                 i32, i32, i32, f32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, sz, c_vp]),
+                                 i32, i32, i32, f32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, sz, c_vp]),
     "exl3b_rmsnorm": (i32, [c_vp, i64, c_vp, i64, c_vp, c_vp, i64, i32, i32, f32, c_vp]),
     "exl3b_rope_neox": (i32, [c_vp, i64, c_vp, i64, i32, i32, i32, c_vp, c_vp, i64, c_vp]),
     "exl3b_silu_mul": (i32, [c_vp, i64, c_vp, i64, i32, i32, c_vp]),

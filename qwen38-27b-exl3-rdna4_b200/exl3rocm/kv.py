@@ -13,6 +13,12 @@ reference runs for ``int8_per_token_head``.
 
 The RHT sign vector is a fixed seeded +-1 vector (``rht_signs``); writes and reads share it, so the
 cache is self-consistent.  There is no CPU path: every call runs on the CUDA library.
+
+Centering (kv_int4.py:120-158): with per-layer K/V channel means (``set_kv_means``, or a file named by
+EXL3_KV_MEANS in the reference's ``{layer: {"k": [kv_heads, 128], "v": ...}}`` format), the int4 write
+adds the rotated-domain biases -(mean @ diag(s) H) before quantising and the attention adds the value
+mean back to its output.  Softmax ignores a per-query constant on the keys, so centering changes only
+how tight the 4-bit ranges are.  Without means nothing is centred.
 """
 from __future__ import annotations
 
@@ -30,6 +36,8 @@ MAX_ROWS = 32  # query rows (query tokens x GQA heads) one attention call takes 
 RHT_SEED = 0x5EED1234
 
 _signs: dict = {}
+_means: dict | None = None  # layer name -> {"k": [kv_heads, 128], "v": ...} (cpu fp32)
+_bias: dict = {}            # (layer name, device) -> device biases, or None
 _exact: dict = {}
 _ws: dict = {}
 _req = {"slot": None, "rows": 0}
@@ -40,7 +48,7 @@ def _stream(device) -> int:
 
 
 def _capturing() -> bool:
-    return torch.cuda.is_current_stream_capturing()
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
 
 
 def rht_signs(device, d: int = HEAD_SIZE) -> torch.Tensor:
@@ -50,6 +58,52 @@ def rht_signs(device, d: int = HEAD_SIZE) -> torch.Tensor:
         bits = np.random.default_rng(RHT_SEED).integers(0, 2, size=d)
         _signs[key] = torch.from_numpy(np.where(bits == 1, 1.0, -1.0).astype(np.float32)).to(device)
     return _signs[key]
+
+
+def set_kv_means(means: dict | None) -> None:
+    """Per-layer channel means {layer_name: {"k": [kv_heads, 128], "v": [kv_heads, 128]}} for the int4
+    centering; None clears them (and the biases derived from them)."""
+    global _means
+    _means = {name: {"k": torch.as_tensor(m["k"], dtype=torch.float32).cpu(),
+                     "v": torch.as_tensor(m["v"], dtype=torch.float32).cpu()} for name, m in (means or {}).items()}
+    _bias.clear()
+
+
+def _load_means() -> dict:
+    """The means set by set_kv_means, else those of the file EXL3_KV_MEANS names (unset or "0": none)."""
+    global _means
+    if _means is None:
+        path = os.environ.get("EXL3_KV_MEANS", "0")
+        set_kv_means(torch.load(path, map_location="cpu") if path != "0" and os.path.exists(path) else {})
+    return _means
+
+
+def layer_bias(name, kv_heads: int, device, d: int = HEAD_SIZE):
+    """The layer's centering terms on the device: {"k", "v"}: rotated-domain write biases
+    -(mean @ diag(s) H) fp32 [kv_heads, d]; "v_mean": the value mean [kv_heads, d] the attention adds
+    back.  None when the layer has no means of this shape.  The first call per layer must be eager."""
+    if not name:
+        return None
+    key = (name, str(device))
+    if key not in _bias:
+        m = _load_means().get(name)
+        if m is None or tuple(m["k"].shape) != (kv_heads, d):
+            _bias[key] = None
+        else:
+            if _capturing():
+                raise RuntimeError("exl3rocm.kv: first use of a layer's means during graph capture")
+            fwd = rht_signs("cpu", d)[:, None] * _sylvester(d)  # x @ fwd == H (x * s), the write's rotation
+            _bias[key] = {"k": (-(m["k"] @ fwd)).to(device), "v": (-(m["v"] @ fwd)).to(device),
+                          "v_mean": m["v"].to(device).contiguous()}
+    return _bias[key]
+
+
+def _sylvester(d: int) -> torch.Tensor:
+    """Natural-order Sylvester Hadamard matrix of +-1 (H[i, j] = (-1)^popcount(i & j))."""
+    h = torch.ones((1, 1), dtype=torch.float32)
+    while h.shape[0] < d:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return h
 
 
 # ---------------------------------------------------------------------------------------------
@@ -180,10 +234,12 @@ def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, *, k_sca
     use_ex = ex is not None and num_seqs > 0
     qsl = query_start_loc.to(torch.int32) if use_ex and query_start_loc.dtype != torch.int32 else query_start_loc
     sl = seq_lens.to(torch.int32) if use_ex and seq_lens.dtype != torch.int32 else seq_lens
+    bias = layer_bias(layer_name, heads, key.device)
     _lib.call("exl3b_kv_int4_write", key.data_ptr(), value.data_ptr(), _dtype_code(key), n, heads, HEAD_SIZE,
               key.stride(0), key.stride(1), value.stride(0), value.stride(1), key_cache.data_ptr(),
               value_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(), slots.data_ptr(),
-              key_cache.shape[1], rht_signs(key.device).data_ptr(), None, None,
+              key_cache.shape[1], rht_signs(key.device).data_ptr(),
+              bias["k"].data_ptr() if bias else None, bias["v"].data_ptr() if bias else None,
               qsl.data_ptr() if use_ex else None, sl.data_ptr() if use_ex else None,
               _req["slot"].data_ptr() if use_ex else None, num_seqs,
               ex["k"].data_ptr() if use_ex else None, ex["v"].data_ptr() if use_ex else None,
@@ -223,10 +279,11 @@ def _attn(kind, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table
         return
     ex = _exact.get(layer_name) if layer_name else None
     use_ex = ex is not None and _req["slot"] is not None
+    bias = layer_bias(layer_name, hkv, q.device)
     _lib.call("exl3b_kv_int4_attn", *common, rht_signs(q.device).data_ptr(),
               ex["k"].data_ptr() if use_ex else None, ex["v"].data_ptr() if use_ex else None,
               ex["tag"].data_ptr() if use_ex else None, _req["slot"].data_ptr() if use_ex else None,
-              ws.data_ptr(), ws.numel(), _stream(q.device))
+              bias["v_mean"].data_ptr() if bias else None, ws.data_ptr(), ws.numel(), _stream(q.device))
 
 
 def attention(*, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale,
@@ -335,6 +392,10 @@ def prefill(orig=None, kw=None, layer_name=None):
         _sdpa_paged(qr, kd, vd, kw["cu_seqlens_q"], kw["seqused_k"], nb, kw["softmax_scale"], rot)
     _lib.call("exl3b_had128", rot.data_ptr(), HEAD_SIZE, out.data_ptr(), HEAD_SIZE, q.numel() // HEAD_SIZE,
               HEAD_SIZE, None, s16.data_ptr(), 1.0, _stream(q.device))  # s * H rot / sqrt(128)
+    bias = layer_bias(layer_name, k.shape[2], q.device)
+    if bias is not None:  # the centering's value mean (kv_int4.py:621), here after the fp16 un-rotation
+        g = q.shape[1] // k.shape[2]
+        out.add_(bias["v_mean"].repeat_interleave(g, dim=0).to(out.dtype))
 
 
 def prefill_int8(orig=None, kw=None):
