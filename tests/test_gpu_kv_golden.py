@@ -6,7 +6,7 @@
    bit-exact and scale words as in tests/test_kv_golden.py, attention within nRMS 2e-3 / cos 0.9999.
 2. At the BASELINE contexts (32k and 64k tokens, B = 1; 4k, B = 8), int8: vLLM's own Triton write and
    unified attention, compiled for this GPU, side by side with this library on the same inputs (writes
-   bit-exact, attention within the gate).  int4: the kernels against the oracle (pinned to the
+   equal up to the GPU's approximate division in vLLM's build, attention within the gate).  int4: the kernels against the oracle (pinned to the
    reference by the fixtures) — codes re-derived for a sample of rows, attention over the whole context.
 """
 from __future__ import annotations
@@ -207,10 +207,17 @@ def test_int8_long_context_matches_vllm_triton(xkv, ctx, batch):
         else:
             xkv.reshape_and_cache_int8(key, val, kc, vc, slots, ks, vs)
         caches.append((kc, vc, ks, vs))
-    (a, b, c, d), (e, f, h, i) = caches
-    assert torch.equal(a, e) and torch.equal(b, f) and torch.equal(c, h) and torch.equal(d, i)
+    # vLLM's Triton build divides with the GPU's approximate fp32 division (the fixtures, run with IEEE
+    # division, are bit-exact): scales agree within 2 units in the last place, and a code may sit one
+    # step away where x / scale lands next to an integer
+    for (cv, sv), (co, so) in (((caches[0][0], caches[0][2]), (caches[1][0], caches[1][2])),
+                               ((caches[0][1], caches[0][3]), (caches[1][1], caches[1][3]))):
+        rel = ((sv - so).abs() / so.abs().clamp_min(1e-30)).max().item()
+        dq = (cv.int() - co.int()).abs()
+        frac = (dq > 0).float().mean().item()
+        assert rel <= 2.5e-7 and dq.max().item() <= 1 and frac <= 1e-3, (rel, dq.max().item(), frac)
     kc, vc, ks, vs = caches[1]
-    del caches, a, b, c, d
+    del caches
     gen = torch.Generator(device=DEV)
     gen.manual_seed(99 + ctx)
     q = torch.randn((batch, HQ, D), generator=gen, device=DEV).half()
