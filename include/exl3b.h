@@ -117,6 +117,23 @@ EXL3B_API int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, 
                          const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* Workspace of exl3b_gemm: a 256-byte header (error word at offset 0) plus A_had [m][k] fp16. */
+EXL3B_API size_t exl3b_gemm_workspace_bytes(int m, int k);
+
+/* The EXL3 linear for any number of rows m >= 1, built for prefill (m in the hundreds and thousands):
+ *   y[m][n] = had_out( fp16( had_in(x, suh) @ W ), svh )
+ * on the 5th-generation tensor cores: had_in into the workspace, then one persistent kernel whose CTAs
+ * decode the trellis tiles of their 256 x 256 output tile into shared memory and feed them to
+ * tcgen05.mma (fp32 accumulation in tensor memory); the epilogue rounds to fp16, applies had_out and
+ * svh.  W never exists in global memory.  x fp16 [m][k] contiguous (16-byte aligned), trellis
+ * [k/16][n/16][16K], suh [k], svh [n], y rows of stride ldy (ldy % 8 == 0, 16-byte aligned).
+ * k % 128 == 0, n % 128 == 0, 1 <= K <= 8, codebook 0..2 (EXL3B_X_BF16 is declined: cast x first).
+ * Replaces the reference's M > 16 route had_r_128 + reconstruct[_slice] + hgemm_recon
+ * (vllm_plugin/exl3rocm/ops.py:86-97), which materialises W and accumulates in fp16. */
+EXL3B_API int exl3b_gemm(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K, int codebook,
+                         const uint16_t* suh, const uint16_t* svh, uint16_t* y, int64_t ldy, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* exl3b_linear_grouped with the RMSNorm before it fused in (vLLM rms_norm): the groups run on
  *   h = fp16( fp16(x * rsqrt(mean(x^2) + eps)) * norm_weight )      (mean in fp32, per row)
  * where x [m][k] is the un-normalised input (the residual stream).  norm_weight fp16 [k].  Rows stay

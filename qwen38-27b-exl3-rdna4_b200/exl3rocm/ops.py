@@ -4,9 +4,10 @@
 implementations for tracing.
 
 Routing by the number of rows M (reference ops.py:80-97):
-  M <= 16  one fused launch pair: had_in -> decode + mma + stream-K reduce + had_out (+ svh)
-  M  > 16  had_in (exl3b_had128) -> dequantised fp16 W in a reserved buffer (exl3b_dequant) ->
-           dense GEMM -> had_out (exl3b_had128), the reference's reconstruct + hgemm route.
+  M <= 16  one fused GEMV launch: had_in -> decode + mma + stream-K reduce + had_out (+ svh)
+  M  > 16  exl3b_gemm: had_in into a workspace, then the tcgen05 GEMM whose CTAs decode the trellis
+           into shared memory (W never materialised) with had_out + svh in its epilogue; it replaces
+           the reference's reconstruct + hgemm route.
 
 The helpers ``decode``, ``reconstruct``, ``reconstruct_slice`` and ``had_r_128`` mirror the fork's
 pybind functions the reference tests call (tests/test_gpu_parity.py:101-139).
@@ -27,7 +28,8 @@ Y_ADD = 0x400  # EXL3B_Y_ADD: y = fp16(y + result), the residual add in the epil
 RECON_SLICE_N = 17408  # widest model layer, as the reference (ops.py:22-24)
 
 _ws: dict = {}    # (device index, stream handle) -> uint8 workspace (counters zeroed once)
-_wbuf: dict = {}  # device -> fp16 reconstruction buffer for the M > 16 route
+_gws: dict = {}   # (device index, stream handle) -> uint8 workspace of the M > 16 GEMM (A_had)
+_wbuf: dict = {}  # device -> fp16 reconstruction buffer (reconstruct / reconstruct_slice)
 
 
 def _stream(device: torch.device) -> int:
@@ -73,6 +75,24 @@ def workspace_error(device=None) -> int:
     out = _lib.i32(0)
     _lib.call("exl3b_linear_workspace_error", ws.data_ptr(), _lib.ctypes.byref(out), _stream(device))
     return int(out.value)
+
+
+def gemm_workspace_bytes(m: int, k: int) -> int:
+    return int(_lib.lib().exl3b_gemm_workspace_bytes(m, k))
+
+
+def reserve_gemm_workspace(device, m: int, k: int, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Grow (never shrink) the M > 16 GEMM workspace of (device, stream) to fit m rows of k inputs."""
+    device = torch.device(device)
+    key = (device.index, (stream or torch.cuda.current_stream(device)).cuda_stream)
+    need = gemm_workspace_bytes(m, k)
+    ws = _gws.get(key)
+    if ws is None or ws.numel() < need:
+        if _capturing():
+            raise RuntimeError("exl3rocm: GEMM workspace too small during graph capture; "
+                               "call reserve_gemm_workspace() for this shape before capturing")
+        _gws[key] = ws = torch.zeros(need, dtype=torch.uint8, device=device)
+    return ws
 
 
 def reserve_weight_buffer(device, numel: int) -> None:
@@ -175,18 +195,15 @@ def _prep_x(x: torch.Tensor, k: int, keep_bf16: bool = False) -> torch.Tensor:
 
 def _linear_large(x2: torch.Tensor, trellis: torch.Tensor, suh, svh, K: int, mcg: bool, mul1: bool,
                   y: torch.Tensor) -> None:
-    """M > 16: transform, dequantise into the reserved buffer, dense GEMM, transform."""
+    """M > 16: the tcgen05 GEMM (exl3b_gemm), y a [M, n] view with unit column stride."""
     M, k = x2.shape
     n = svh.shape[0]
-    xh = torch.empty_like(x2)
-    had_r_128(x2, xh, suh, None, 1.0)
-    for n0 in range(0, n, RECON_SLICE_N):
-        n1 = min(n0 + RECON_SLICE_N, n)
-        w = _weight_buffer(x2.device, k * (n1 - n0)).view(k, n1 - n0)
-        reconstruct_slice(w, trellis, K, mcg, mul1, n0)
-        torch.mm(xh, w, out=y[:, n0:n1]) if y.is_contiguous() and (n0, n1) == (0, n) else \
-            y[:, n0:n1].copy_(torch.mm(xh, w))
-    had_r_128(y, y, None, svh, 1.0)
+    if x2.data_ptr() % 16:
+        x2 = x2.clone()
+    assert y.stride(1) == 1 and y.data_ptr() % 16 == 0 and y.stride(0) % 8 == 0
+    ws = reserve_gemm_workspace(x2.device, M, k)
+    _lib.call("exl3b_gemm", x2.data_ptr(), M, k, trellis.data_ptr(), n, K, _cb(mcg, mul1), suh.data_ptr(),
+              svh.data_ptr(), y.data_ptr(), y.stride(0), ws.data_ptr(), ws.numel(), _stream(x2.device))
 
 
 # ---------------------------------------------------------------------------------------------
