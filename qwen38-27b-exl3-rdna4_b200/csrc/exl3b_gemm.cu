@@ -107,9 +107,12 @@ EXL3B_DEV uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
 EXL3B_DEV void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
-// arrive on an mbarrier of another CTA of the cluster, releasing this thread's writes at cluster scope
+// arrive on an mbarrier of a CTA of the cluster (its shared::cluster address).  The default semantics
+// (release at CTA scope) suffice: what the waiter consumes is shared memory read by the tensor core,
+// made visible by fence.proxy.async before the arrive; a cluster-scope release here cost a third of
+// the kernel's time (measured: 471 -> 347 us at M 2048, 5120 -> 17408).
 EXL3B_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" :: "r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" :: "r"(cluster_addr) : "memory");
 }
 
 EXL3B_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
