@@ -316,30 +316,94 @@ def bench_kv(torch, dev, kind: int, ctx: int, batch: int, q_len: int, iters: int
             "gb_s": kv_bytes / (ms * 1e-3) / 1e9, "kv_bytes": kv_bytes}
 
 
-def bench_prefill(torch, dev, K: int, m: int = 2048, iters: int = 5) -> dict:
-    """One gate_up-shaped EXL3 linear (5120 -> 17408) at M rows through the public op."""
+def _layer_weights(torch, dev, k, n, K, seed):
     g = torch.Generator(device=dev)
-    g.manual_seed(5)
-    tr = torch.randint(-32768, 32768, (HIDDEN // 16, INTER // 16, 16 * K), generator=g, device=dev,
+    g.manual_seed(seed)
+    tr = torch.randint(-32768, 32768, (k // 16, n // 16, 16 * K), generator=g, device=dev,
                        dtype=torch.int32).to(torch.int16)
-    suh = (torch.randint(0, 2, (HIDDEN,), generator=g, device=dev) * 2 - 1).half()
-    svh = (torch.randint(0, 2, (INTER,), generator=g, device=dev) * 2 - 1).half()
-    x = torch.randn((m, HIDDEN), generator=g, device=dev).to(torch.bfloat16)
-    from exl3rocm import ops as xops
-    xops.reserve_weight_buffer(dev, HIDDEN * INTER)
-    torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, True)
+    suh = (torch.randint(0, 2, (k,), generator=g, device=dev) * 2 - 1).half()
+    svh = (torch.randint(0, 2, (n,), generator=g, device=dev) * 2 - 1).half()
+    return g, tr, suh, svh
+
+
+def _event_ms(torch, fn, iters, flush=None):
+    """Median event-timed duration of fn() on the current stream (a write larger than L2 between
+    calls when flush is given)."""
     times = []
     for _ in range(iters):
+        if flush is not None:
+            _flush_l2(torch, flush)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, True)
+        fn()
         e1.record()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
-    ms = statistics.median(times)
-    return {"m": m, "k": HIDDEN, "n": INTER, "bits": K, "ms": ms,
-            "tflops": 2.0 * m * HIDDEN * INTER / (ms * 1e-3) / 1e12,
-            "route": "had128 + dequant to fp16 + dense fp16 GEMM (torch.mm) + had128"}
+    return statistics.median(times)
+
+
+def bench_prefill(torch, dev, K: int, m: int = 2048, iters: int = 10, peak_tflops: float = 1664.8) -> dict:
+    """One gate_up-shaped EXL3 linear (5120 -> 17408) at M rows through the public op (the tcgen05 GEMM
+    of exl3b_gemm: had_in, then the trellis decoded into shared memory feeding tcgen05.mma), with the
+    L2 flushed before every call.  Beside it, the reference's own route on this GPU's libraries
+    (had_in, reconstruct into a dense fp16 W, cuBLAS GEMM, had_out: ops.py:86-97) on the same inputs,
+    for comparison only."""
+    from exl3rocm import ops as xops
+    g, tr, suh, svh = _layer_weights(torch, dev, HIDDEN, INTER, K, 5)
+    x = torch.randn((m, HIDDEN), generator=g, device=dev).to(torch.bfloat16)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    op = lambda: torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, True)
+    op()
+    ms = _event_ms(torch, op, iters, flush)
+    # the dense-W route of the reference, with cuBLAS (not this library's product path)
+    w = torch.empty(HIDDEN, INTER, dtype=torch.float16, device=dev)
+    xh = torch.empty((m, HIDDEN), dtype=torch.float16, device=dev)
+    y = torch.empty((m, INTER), dtype=torch.float16, device=dev)
+
+    def dense_route():
+        xops.had_r_128(x.half(), xh, suh, None, 1.0)
+        xops.reconstruct(w, tr, K, False, True)
+        torch.mm(xh, w, out=y)
+        xops.had_r_128(y, y, None, svh, 1.0)
+    dense_route()
+    ms_dense = _event_ms(torch, dense_route, iters, flush)
+    del w, xh, y, flush
+    fl = 2.0 * m * HIDDEN * INTER
+    tf = fl / (ms * 1e-3) / 1e12
+    return {"m": m, "k": HIDDEN, "n": INTER, "bits": K, "ms": ms, "tflops": tf,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak_tflops, "unit": "TFLOP/s",
+                         "frac": tf / peak_tflops, "flops_per_call": fl},
+            "route": "exl3b_gemm: had_in, then tcgen05 GEMM (cta_group::2) over trellis decoded in shared memory",
+            "dense_w_cublas_route": {"ms": ms_dense, "tflops": fl / (ms_dense * 1e-3) / 1e12}}
+
+
+SWEEP_SHAPES = [("q/o", HIDDEN, HIDDEN), ("k/v", HIDDEN, KV_HEADS * HEAD_DIM), ("gate/up", HIDDEN, INTER),
+                ("down", INTER, HIDDEN)]
+
+
+def bench_sweep(torch, dev, rows=(1, 4, 8, 16, 128, 2048), bits=(2, 3, 4, 5, 6, 8), iters: int = 10) -> list:
+    """The M / bit-width sweep on the layer shapes, through the public op, L2 flushed between calls:
+    every M at 4 bits on every shape, and every bit width at M = 1 and M = 2048 on gate/up.
+    M <= 16 reports GB/s of algorithmic bytes (HBM-bound GEMV), M >= 128 TFLOP/s (tensor-bound GEMM)."""
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    points = [(nm, k, n, m, 4) for nm, k, n in SWEEP_SHAPES for m in rows]
+    points += [("gate/up", HIDDEN, INTER, m, K) for K in bits if K != 4 for m in (1, 2048)]
+    out = []
+    for nm, k, n, m, K in points:
+        g, tr, suh, svh = _layer_weights(torch, dev, k, n, K, 7 + k + n + K)
+        x = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+        op = lambda: torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, True)
+        op()
+        ms = _event_ms(torch, op, iters, flush)
+        rec = {"shape": nm, "k": k, "n": n, "m": m, "bits": K, "ms": ms}
+        if m <= 16:
+            rec["gb_s"] = linear_bytes(k, n, K, m) / (ms * 1e-3) / 1e9
+        else:
+            rec["tflops"] = 2.0 * m * k * n / (ms * 1e-3) / 1e12
+        out.append(rec)
+        del tr, suh, svh, x
+    del flush
+    return out
 
 
 def bench_decode(torch, dev, steps: int, warmup: int, ctx: int = 32768,
@@ -615,7 +679,8 @@ def main():
         extra["kv_attention"] = [bench_kv(torch, dev, kind, ctx, b, ql)
                                  for kind, ctx, b, ql in ((8, 32768, 8, 1), (4, 32768, 8, 1), (8, 32768, 1, 4),
                                                           (4, 65536, 1, 1), (8, 4096, 8, 1), (8, 32768, 1, 1))]
-        extra["prefill_m2048"] = bench_prefill(torch, dev, K)
+        extra["prefill_m2048"] = bench_prefill(torch, dev, K, peak_tflops=float(peaks.get("bf16_tflops", 1590.0)))
+        extra["sweep"] = bench_sweep(torch, dev)
 
     if not args.no_extra and not args.no_decode and (world == 1 or comm is not None):
         del layers, outs, inputs

@@ -13,16 +13,16 @@
 // columns 128 r .. of B, and its tensor memory receives its rows of both 256 x 256 accumulators (512
 // columns).  Each CTA therefore decodes half of the weight tile, and reads half of B per MMA from its
 // shared memory.  Per 64-input k-block, in each CTA:
-//   * warp 16 (producer) streams the CTA's trellis bytes (four k-rows of eight 16x16 tiles, one bulk
+//   * warp 8 (producer) streams the CTA's trellis bytes (four k-rows of eight 16x16 tiles, one bulk
 //     copy per k-row) into a raw ring, and its two 128-row A_had sub-tiles by TMA (128-byte swizzle),
 //     counted on the leader CTA's barrier;
-//   * warps 0-15 decode the 32 trellis tiles (two each; the lane placement of mma.m16n8k16's A
+//   * warps 0-7 decode the 32 trellis tiles (four each; the lane placement of mma.m16n8k16's A
 //     operand, see exl3b_common.cuh) and store the fp16 weights K-major with the same swizzle, the
 //     layout the MMA's shared-memory descriptors describe; they arrive on the leader's barrier;
-//   * in the leader, warp 17 issues 2 x 4 tcgen05.mma (cta_group::2) and commits to the barriers of
+//   * in the leader, warp 9 issues 2 x 4 tcgen05.mma (cta_group::2) and commits to the barriers of
 //     both CTAs that free the stages.
-// After the last k-block every CTA's warps 0-15 read their accumulator rows back (warp w: TMEM lanes
-// 32 (w % 4) .., accumulator w / 8, 128-column block (w / 4) % 2), one output row per thread: fp16
+// After the last k-block every CTA's warps 0-7 read their accumulator rows back (task t = w, w + 8:
+// TMEM lanes 32 (t % 4) .., accumulator t / 8, 128-column block (t / 4) % 2), one output row per thread: fp16
 // round (the reference's c_rot), the 128-point Hadamard of the block (H4 x H32 through tensor memory),
 // 1/sqrt(128), fp16, times svh (fp16), stored.
 //
@@ -41,10 +41,18 @@ constexpr int kBN = 256;            // output columns per tile (the MMA's N)
 constexpr int kHalfN = kBN / 2;     // B columns held (and decoded) by one CTA
 constexpr int kBK = 64;             // inputs per k-block (one 128-byte swizzle row of fp16)
 constexpr int kSubRows = 128;       // rows of one A sub-tile / of one CTA's share of an accumulator
-constexpr int kDecodeWarps = 16;
-constexpr int kProducerWarp = 16;
-constexpr int kMmaWarp = 17;
-constexpr int kThreads = 32 * 18;
+#ifndef EXL3B_GEMM_DECODE_WARPS
+#define EXL3B_GEMM_DECODE_WARPS 8
+#endif
+// 8 decode warps of four tiles each per k-block measured faster than 16 of two (the per-k-block
+// barrier traffic is the same per warp): 347 -> 326 us at M 2048, 5120 -> 17408
+constexpr int kDecodeWarps = EXL3B_GEMM_DECODE_WARPS;   // 8 or 16
+constexpr int kTilesPerWarp = 32 / kDecodeWarps;        // trellis tiles one decode warp takes per k-block
+constexpr int kTasksPerWarp = 16 / kDecodeWarps;        // epilogue (lane quarter, accumulator, block) tasks
+constexpr int kProducerWarp = kDecodeWarps;
+constexpr int kMmaWarp = kDecodeWarps + 1;
+constexpr int kThreads = 32 * (kDecodeWarps + 2);
+static_assert(kDecodeWarps == 8 || kDecodeWarps == 16, "decode warps");
 constexpr int kAStages = 4;
 constexpr int kBStages = 3;
 constexpr int kRawStages = 4;
@@ -378,7 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         geom.init(lane);
         const int g = lane >> 2, c = lane & 3;
         const int nt16 = p.n / 16;
-        const int ntl = warp & 7, kt0 = 2 * (warp >> 3);  // this warp's n-tile and first of its two k-tiles
+        // this warp's n-tile and the first of its kTilesPerWarp k-tiles
+        const int ntl = warp & 7, kt0 = kTilesPerWarp * (warp >> 3);
         // byte offset inside a B stage of register r of this lane's fragment for k-tile kt: row
         // n = 16 ntl + g + 8 (r & 1), input k = 16 kt + 2c + 8 (r >> 1)
         auto b_off = [&](int kt, int r) -> uint32_t {
@@ -402,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 uint8_t* bst = smem + S::kB + bs * kBStage;
                 if (ntl < nv) {
 #pragma unroll
-                    for (int j = 0; j < 2; ++j) {
+                    for (int j = 0; j < kTilesPerWarp; ++j) {
                         const int kt = kt0 + j;
                         const uint8_t* tb = raw + kt * S::kRawRow + ntl * S::kTile;
                         uint32_t W[LaneGeom<K>::kNW];
@@ -427,8 +436,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             //      128 ((w / 4) % 2) ..: one row and one 128-column block per thread ----
             if (!warp_wait(acc_full, tcount & 1, p.err, 0x323, abort_flag)) break;
             tc_fence_after();
-            {
-                const int lq = warp & 3, task = warp >> 2, sub = task >> 1, blk = task & 1;
+#pragma unroll 1
+            for (int tk = 0; tk < kTasksPerWarp; ++tk) {
+                // task ids keep warp % 4: a warp may only access TMEM lanes 32 (warp % 4) ..
+                const int tid = warp + tk * kDecodeWarps;
+                const int lq = tid & 3, task = tid >> 2, sub = task >> 1, blk = task & 1;
                 const int row = pm * kPairRows + sub * 256 + (int)rank * kSubRows + lq * 32 + lane;
                 const int col0 = pn * kBN + blk * 128;
                 const uint32_t tbase = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(sub * kBN + blk * 128);
