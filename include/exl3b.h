@@ -152,7 +152,18 @@ EXL3B_API int exl3b_linear_grouped_rmsnorm(const uint16_t* x, int m, int k, int 
  * is stored in the scale's low 4 mantissa bits).  key/value inputs are [tokens][heads][128] with
  * the given strides (elements), dtype 0 = fp16, 1 = bf16.  slot_mapping[t] = block * block_size +
  * offset, negative = skip.
+ *
+ * Every KV call takes an optional layout (NULL = the dense layout above).  vLLM's per-token-head caches
+ * (kv_cache [num_blocks][2][block_size][Hkv][row bytes + 4], the fp32 scale inline after each row, the
+ * K and V halves interleaved per block; vllm/v1/attention/backends/triton_attn.py _ensure_scale_caches)
+ * are described by their strides: cache strides in bytes (multiples of 4, head stride >= the row bytes)
+ * and scale strides in floats.  Rows that all start on 16-byte boundaries are read with 16-byte copies,
+ * others with 4-byte ones.
  * ------------------------------------------------------------------------------------------ */
+typedef struct {
+    int64_t cache_block, cache_slot, cache_head; /* bytes */
+    int64_t scale_block, scale_slot, scale_head; /* floats */
+} exl3b_kv_layout;
 
 /* int8 per-token-head quantize-on-write: scale = max(absmax/127, 1e-6), q = trunc(clamp(x/scale)).
  * Replaces vLLM's triton_reshape_and_cache_flash_per_token_head_quant, which the reference's
@@ -161,7 +172,7 @@ EXL3B_API int exl3b_kv_int8_write(const void* key, const void* value, int dtype,
                                   int num_kv_heads, int head_size, int64_t k_stride_tok, int64_t k_stride_head,
                                   int64_t v_stride_tok, int64_t v_stride_head, int8_t* key_cache,
                                   int8_t* value_cache, float* k_scale, float* v_scale, const int64_t* slot_mapping,
-                                  int block_size, void* stream);
+                                  int block_size, const exl3b_kv_layout* layout, void* stream);
 
 /* exl3b_kv_int8_write fused with the neox rotary embedding of the same tokens (exl3b_rope_neox):
  * row t of qkv (fp16, stride ld) holds num_q_heads q heads, then num_kv_heads k heads, then
@@ -173,7 +184,7 @@ EXL3B_API int exl3b_kv_int8_write_rope(const uint16_t* qkv, int64_t ld, uint16_t
                              int64_t num_tokens, int num_q_heads, int num_kv_heads, const int64_t* positions,
                              const float* cos_sin, int64_t max_position, int8_t* key_cache, int8_t* value_cache,
                              float* k_scale, float* v_scale, const int64_t* slot_mapping, int block_size,
-                             void* stream);
+                             const exl3b_kv_layout* layout, void* stream);
 
 /* int4 quantize-on-write: y = H (x * signs) unnormalised (+ optional rotated-domain bias [heads][128]),
  * 3x3 clip search, asymmetric 4 bit, nibble packing.  With exact_tag != NULL also keeps exact fp16 y
@@ -189,7 +200,7 @@ EXL3B_API int exl3b_kv_int4_write(const void* key, const void* value, int dtype,
                                   int block_size, const float* rht_signs, const float* bias_k, const float* bias_v,
                                   const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* seq_slots,
                                   int num_seqs, uint16_t* exact_k, uint16_t* exact_v, int32_t* exact_tag,
-                                  void* stream);
+                                  const exl3b_kv_layout* layout, void* stream);
 
 /* Workspace of the attention calls (split-KV partials; int4 also its rotated q). */
 EXL3B_API size_t exl3b_kv_attn_workspace_bytes(int num_tokens, int num_q_heads, int num_seqs, int num_kv_heads,
@@ -205,7 +216,8 @@ EXL3B_API int exl3b_kv_int8_attn(const uint16_t* q, uint16_t* out, int num_token
                                  const float* k_scale, const float* v_scale, int block_size,
                                  const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
                                  const int32_t* query_start_loc, int num_seqs, int max_q_len, int max_seq_len,
-                                 float softmax_scale, void* workspace, size_t workspace_bytes, void* stream);
+                                 float softmax_scale, void* workspace, size_t workspace_bytes,
+                                 const exl3b_kv_layout* layout, void* stream);
 
 /* The same over the int4 cache: q is rotated with the RHT, rows with a matching exact tag (first 4
  * and newest 128 positions of a request slot) are read from the exact fp16 rows, and the output is
@@ -221,13 +233,14 @@ EXL3B_API int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_token
                                  int max_q_len, int max_seq_len, float softmax_scale, const float* rht_signs,
                                  const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
                                  const int32_t* seq_slots, const float* out_bias, void* workspace,
-                                 size_t workspace_bytes, void* stream);
+                                 size_t workspace_bytes, const exl3b_kv_layout* layout, void* stream);
 
 /* Prefill over the quantised caches: gather the blocks listed in block_ids (n entries) and dequantise
  * them to fp16 rows out[n][block_size][num_kv_heads][128], for an fp16 attention kernel to read.
  * int8: out = fp16(q * scale).  Replaces gather_dequant (reference vllm_plugin/exl3rocm/kv_dequant.py:42-152). */
 EXL3B_API int exl3b_kv_int8_gather(const int8_t* cache, const float* scale, int block_size, int num_kv_heads,
-                                   int head_size, const int32_t* block_ids, int64_t n, uint16_t* out, void* stream);
+                                   int head_size, const int32_t* block_ids, int64_t n, uint16_t* out,
+                                   const exl3b_kv_layout* layout, void* stream);
 /* int4: out = fp16((nibble - zp) * scale / sqrt(128)), still rotated but in the orthonormal domain;
  * block_ids lists blocks_per_seq blocks per sequence, and with exact_tag given, positions whose exact row
  * (first 4 / newest 128 of the sequence's request slot) carries a matching tag take that row / sqrt(128).
@@ -236,7 +249,8 @@ EXL3B_API int exl3b_kv_int8_gather(const int8_t* cache, const float* scale, int 
 EXL3B_API int exl3b_kv_int4_gather(const uint8_t* cache, const float* scale, int block_size, int num_kv_heads,
                                    int head_size, const int32_t* block_ids, int64_t n, int blocks_per_seq,
                                    uint16_t* out, const uint16_t* exact, const int32_t* exact_tag,
-                                   const int32_t* seq_slots, const int32_t* seq_lens, void* stream);
+                                   const int32_t* seq_slots, const int32_t* seq_lens, const exl3b_kv_layout* layout,
+                                   void* stream);
 
 /* exl3b_linear without a caller-provided workspace, for callers that cannot allocate device
  * memory: code that runs while a CUDA graph is being captured (cudaMalloc is not allowed there),

@@ -36,6 +36,17 @@ constexpr int kMaxSplits = 256;  // the reference segments at most 64 ways (kv_i
 // every record starts on a 16-byte boundary (the kernels move it as float4)
 constexpr int kPartialStride = kHD + 4;
 
+// Where the (block, slot, head) row of a paged cache and its fp32 scale live.  Dense caches hold rows
+// of R bytes at [blocks][block_size][H] and scales at [blocks][block_size][H]; vLLM's per-token-head
+// caches keep each row's scale inline after it and interleave the K and V halves of every block, so
+// the host passes their strides.
+struct KvLayout {
+    int64_t blk, slot, head;     // cache strides in bytes
+    int64_t sblk, sslot, shead;  // scale strides in floats
+    EXL3B_DEV int64_t row(int64_t b, int64_t o, int h) const { return b * blk + o * slot + (int64_t)h * head; }
+    EXL3B_DEV int64_t srow(int64_t b, int64_t o, int h) const { return b * sblk + o * sslot + (int64_t)h * shead; }
+};
+
 EXL3B_DEV float load_in(const void* p, int64_t i, int dtype) {
     return dtype == 0 ? __half2float(reinterpret_cast<const __half*>(p)[i])
                       : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
@@ -67,6 +78,7 @@ struct KvWriteArgs {
     void* key_cache; void* value_cache; float* k_scale; float* v_scale;
     const int64_t* slot_mapping;
     int num_tokens, num_heads, block_size;
+    KvLayout lay;
 };
 
 EXL3B_DEV void int8_quant_store(const float (&x)[4], int8_t* dst, float* scale_dst, int lane) {
@@ -91,15 +103,15 @@ __global__ void kv_int8_write_kernel(const KvWriteArgs a) {
     const int64_t slot = a.slot_mapping[t];
     if (slot < 0) return;
     const int64_t blk = slot / a.block_size, off = slot % a.block_size;
-    const int64_t row = (blk * a.block_size + off) * a.num_heads + h;
+    const int64_t row = a.lay.row(blk, off, h), srow = a.lay.srow(blk, off, h);
     float xk[4], xv[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         xk[i] = load_in(a.key, t * a.k_stride_tok + h * a.k_stride_head + 4 * lane + i, a.dtype);
         xv[i] = load_in(a.value, t * a.v_stride_tok + h * a.v_stride_head + 4 * lane + i, a.dtype);
     }
-    int8_quant_store(xk, reinterpret_cast<int8_t*>(a.key_cache) + row * kHD, a.k_scale + row, lane);
-    int8_quant_store(xv, reinterpret_cast<int8_t*>(a.value_cache) + row * kHD, a.v_scale + row, lane);
+    int8_quant_store(xk, reinterpret_cast<int8_t*>(a.key_cache) + row, a.k_scale + srow, lane);
+    int8_quant_store(xv, reinterpret_cast<int8_t*>(a.value_cache) + row, a.v_scale + srow, lane);
 }
 
 // The same write fused with the neox rotary embedding of the token's q and k (a decode step's qkv
@@ -153,7 +165,7 @@ __global__ void kv_int8_write_rope_kernel(const KvWriteArgs a, const KvRopeArgs 
     const int64_t slot = a.slot_mapping[t];
     if (slot < 0) return;
     const int64_t blk = slot / a.block_size, off = slot % a.block_size;
-    const int64_t row = (blk * a.block_size + off) * a.num_heads + h;
+    const int64_t row = a.lay.row(blk, off, h), srow = a.lay.srow(blk, off, h);
     const uint2 wk = *reinterpret_cast<const uint2*>(row_in + (r.nq + h) * kHD + 4 * lane);
     const uint2 wv = *reinterpret_cast<const uint2*>(row_in + (r.nq + a.num_heads + h) * kHD + 4 * lane);
     float xk[4] = {__low2float(u32_as_h2(wk.x)), __high2float(u32_as_h2(wk.x)), __low2float(u32_as_h2(wk.y)),
@@ -165,8 +177,8 @@ __global__ void kv_int8_write_rope_kernel(const KvWriteArgs a, const KvRopeArgs 
 #pragma unroll
         for (int e = 0; e < 4; ++e) xk[e] = __half2float(__float2half_rn(xk[e]));
     }
-    int8_quant_store(xk, reinterpret_cast<int8_t*>(a.key_cache) + row * kHD, a.k_scale + row, lane);
-    int8_quant_store(xv, reinterpret_cast<int8_t*>(a.value_cache) + row * kHD, a.v_scale + row, lane);
+    int8_quant_store(xk, reinterpret_cast<int8_t*>(a.key_cache) + row, a.k_scale + srow, lane);
+    int8_quant_store(xv, reinterpret_cast<int8_t*>(a.value_cache) + row, a.v_scale + srow, lane);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -253,11 +265,10 @@ __global__ void kv_int4_write_kernel(const KvWriteArgs a, const KvInt4Extra x) {
     uint32_t sbits;
     int4_quant_row(v, code, sbits);
     const int64_t blk = slot / a.block_size, off = slot % a.block_size;
-    const int64_t row = (blk * a.block_size + off) * a.num_heads + h;
-    uint8_t* cache = reinterpret_cast<uint8_t*>(side ? a.value_cache : a.key_cache) + row * (kHD / 2);
+    uint8_t* cache = reinterpret_cast<uint8_t*>(side ? a.value_cache : a.key_cache) + a.lay.row(blk, off, h);
     const uint16_t packed = (uint16_t)((code[0] | (code[1] << 4)) | ((code[2] | (code[3] << 4)) << 8));
     reinterpret_cast<uint16_t*>(cache)[lane] = packed;
-    if (lane == 0) (side ? a.v_scale : a.k_scale)[row] = __uint_as_float(sbits);
+    if (lane == 0) (side ? a.v_scale : a.k_scale)[a.lay.srow(blk, off, h)] = __uint_as_float(sbits);
     // exact rows
     if (x.exact_tag && x.seq_slots) {
         const int s = seq_of_token(x.query_start_loc, x.num_seqs, t);
@@ -315,6 +326,8 @@ struct KvAttnArgs {
     // int4 exact rows
     const __half* exact_k; const __half* exact_v; const int32_t* exact_tag; const int32_t* seq_slots;
     int tsplit;                  // > 1: that many warps share the split's keys (one warp holds all rows)
+    KvLayout lay;
+    int al16;                    // every cache row starts on a 16-byte boundary: 16-byte copies
 };
 
 // int8 word (4 signed bytes) -> two half2 (bytes 0,1) and (bytes 2,3), exact
@@ -498,9 +511,9 @@ __global__ void __launch_bounds__(32 * 4) kv_attn_kernel(const KvAttnArgs a) {
         uint32_t my_slot = 0xFFFFFFFFu;  // block * block_size + slot of token t: fits 32 bits for any cache
         if (t < t_hi) {
             my_slot = ((uint32_t)bt_win[(t >> lg) - win_base] << lg) + (uint32_t)(t & bs_mask);
-            const int64_t row = (int64_t)my_slot * a.num_kv_heads + kvh;
-            cp_async4(tb + 2 * SM::kRows + lane * 4, a.k_scale + row);
-            cp_async4(tb + 2 * SM::kRows + 128 + lane * 4, a.v_scale + row);
+            const int64_t srow = a.lay.srow(my_slot >> lg, my_slot & (uint32_t)bs_mask, kvh);
+            cp_async4(tb + 2 * SM::kRows + lane * 4, a.k_scale + srow);
+            cp_async4(tb + 2 * SM::kRows + 128 + lane * 4, a.v_scale + srow);
         }
         const int ch = lane % C16;
 #pragma unroll
@@ -508,10 +521,20 @@ __global__ void __launch_bounds__(32 * 4) kv_attn_kernel(const KvAttnArgs a) {
             const int r = lane / C16 + (32 / C16) * j;
             const uint32_t sl = __shfl_sync(0xFFFFFFFFu, my_slot, r);
             if (sl != 0xFFFFFFFFu) {
-                const int64_t off = ((int64_t)sl * a.num_kv_heads + kvh) * RB + ch * 16;
+                const int64_t off = a.lay.row(sl >> lg, sl & (uint32_t)bs_mask, kvh) + ch * 16;
                 const uint32_t soff = r * RB + ((ch ^ (r & (C16 - 1))) * 16);
-                cp_async16(tb + soff, reinterpret_cast<const uint8_t*>(a.key_cache) + off);
-                cp_async16(tb + SM::kRows + soff, reinterpret_cast<const uint8_t*>(a.value_cache) + off);
+                const uint8_t* ks = reinterpret_cast<const uint8_t*>(a.key_cache) + off;
+                const uint8_t* vs = reinterpret_cast<const uint8_t*>(a.value_cache) + off;
+                if (a.al16) {
+                    cp_async16(tb + soff, ks);
+                    cp_async16(tb + SM::kRows + soff, vs);
+                } else {  // rows on 4-byte boundaries (scales inline): four 4-byte copies per chunk
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        cp_async4(tb + soff + 4 * w, ks + 4 * w);
+                        cp_async4(tb + SM::kRows + soff + 4 * w, vs + 4 * w);
+                    }
+                }
             }
         }
         cp_async_commit();
@@ -1037,6 +1060,7 @@ struct KvGatherArgs {
     int bs, H, nb;
     __half* out;                 // [n][bs][H][128]
     float mul;                   // int4: 1/sqrt(128), the orthonormal rotated domain; int8: 1
+    KvLayout lay;
     // int4 exact rows (optional): position p of sequence s is exact when its tag matches
     const __half* exact; const int32_t* exact_tag; const int32_t* seq_slots; const int32_t* seq_lens;
 };
@@ -1050,7 +1074,8 @@ __global__ void kv_gather_kernel(const KvGatherArgs a) {
     const int64_t j = item / ((int64_t)a.bs * a.H);
     const int rem = (int)(item - j * a.bs * a.H);
     const int slot = rem / a.H, h = rem % a.H;
-    const int64_t row = ((int64_t)a.block_ids[j] * a.bs + slot) * a.H + h;
+    const int64_t b = a.block_ids[j];
+    const int64_t row = a.lay.row(b, slot, h), srow = a.lay.srow(b, slot, h);
     float v[4];
     bool done = false;
     if (KV == 4 && a.exact_tag) {
@@ -1070,13 +1095,13 @@ __global__ void kv_gather_kernel(const KvGatherArgs a) {
     }
     if (!done) {
         if constexpr (KV == 8) {
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(a.cache + row * kHD + 4 * lane);
-            const float sc = a.scale[row];
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(a.cache + row + 4 * lane);
+            const float sc = a.scale[srow];
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[i] = (float)(int8_t)((w >> (8 * i)) & 0xFFu) * sc;
         } else {
-            const uint16_t w = *reinterpret_cast<const uint16_t*>(a.cache + row * (kHD / 2) + 2 * lane);
-            const uint32_t bits = __float_as_uint(a.scale[row]);
+            const uint16_t w = *reinterpret_cast<const uint16_t*>(a.cache + row + 2 * lane);
+            const uint32_t bits = __float_as_uint(a.scale[srow]);
             const float zp = (float)(bits & 0xFu);
             const float sc = __uint_as_float(bits & 0xFFFFFFF0u) * a.mul;
 #pragma unroll
@@ -1144,10 +1169,32 @@ static int ilog2(int v) { int l = 0; while ((1 << l) < v) ++l; return l; }
 
 using namespace exl3b;
 
+// The device layout of a cache with rows of row_bytes bytes: the caller's strides, or dense.  Rows
+// must sit on 4-byte boundaries; al16 reports whether every row also starts on a 16-byte one.
+static int kv_layout(const exl3b_kv_layout* l, int block_size, int heads, int row_bytes, const void* kc,
+                     const void* vc, KvLayout& out, int& al16) {
+    if (!l) {
+        out.head = row_bytes; out.slot = (int64_t)heads * row_bytes; out.blk = (int64_t)block_size * out.slot;
+        out.shead = 1; out.sslot = heads; out.sblk = (int64_t)block_size * heads;
+    } else {
+        out.blk = l->cache_block; out.slot = l->cache_slot; out.head = l->cache_head;
+        out.sblk = l->scale_block; out.sslot = l->scale_slot; out.shead = l->scale_head;
+        if (out.blk <= 0 || out.slot <= 0 || out.head < row_bytes || out.sblk <= 0 || out.sslot <= 0 ||
+            out.shead <= 0)
+            return EXL3B_BAD_ARG;
+        if (out.blk % 4 || out.slot % 4 || out.head % 4) return EXL3B_BAD_ARG;
+    }
+    if ((kc && !aligned(kc, 4)) || (vc && !aligned(vc, 4))) return EXL3B_BAD_ARG;
+    al16 = out.blk % 16 == 0 && out.slot % 16 == 0 && out.head % 16 == 0 && (!kc || aligned(kc, 16)) &&
+           (!vc || aligned(vc, 16));
+    return EXL3B_OK;
+}
+
 static int kv_write_common(KvWriteArgs& a, const void* key, const void* value, int dtype, int64_t num_tokens,
                            int num_kv_heads, int head_size, int64_t k_stride_tok, int64_t k_stride_head,
                            int64_t v_stride_tok, int64_t v_stride_head, void* key_cache, void* value_cache,
-                           float* k_scale, float* v_scale, const int64_t* slot_mapping, int block_size) {
+                           float* k_scale, float* v_scale, const int64_t* slot_mapping, int block_size,
+                           const exl3b_kv_layout* layout, int row_bytes) {
     if (head_size != kHD || (dtype != 0 && dtype != 1) || block_size <= 0) return EXL3B_DECLINED;
     if (num_tokens < 0 || num_kv_heads <= 0) return EXL3B_BAD_ARG;
     if (num_tokens > 0 && (!key || !value || !key_cache || !value_cache || !k_scale || !v_scale || !slot_mapping))
@@ -1158,18 +1205,19 @@ static int kv_write_common(KvWriteArgs& a, const void* key, const void* value, i
     a.key_cache = key_cache; a.value_cache = value_cache; a.k_scale = k_scale; a.v_scale = v_scale;
     a.slot_mapping = slot_mapping; a.num_tokens = (int)num_tokens; a.num_heads = num_kv_heads;
     a.block_size = block_size;
-    return EXL3B_OK;
+    int al16 = 0;
+    return kv_layout(layout, block_size, num_kv_heads, row_bytes, key_cache, value_cache, a.lay, al16);
 }
 
 extern "C" int exl3b_kv_int8_write(const void* key, const void* value, int dtype, int64_t num_tokens,
                                    int num_kv_heads, int head_size, int64_t k_stride_tok, int64_t k_stride_head,
                                    int64_t v_stride_tok, int64_t v_stride_head, int8_t* key_cache,
                                    int8_t* value_cache, float* k_scale, float* v_scale, const int64_t* slot_mapping,
-                                   int block_size, void* stream) {
+                                   int block_size, const exl3b_kv_layout* layout, void* stream) {
     KvWriteArgs a = {};
     int st = kv_write_common(a, key, value, dtype, num_tokens, num_kv_heads, head_size, k_stride_tok, k_stride_head,
                              v_stride_tok, v_stride_head, key_cache, value_cache, k_scale, v_scale, slot_mapping,
-                             block_size);
+                             block_size, layout, kHD);
     if (st != EXL3B_OK || num_tokens == 0) return st;
     const int64_t items = num_tokens * num_kv_heads;
     kv_int8_write_kernel<<<(unsigned)((items + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a);
@@ -1180,7 +1228,8 @@ extern "C" int exl3b_kv_int8_write_rope(const uint16_t* qkv, int64_t ld, uint16_
                                         int64_t num_tokens, int num_q_heads, int num_kv_heads,
                                         const int64_t* positions, const float* cos_sin, int64_t max_position,
                                         int8_t* key_cache, int8_t* value_cache, float* k_scale, float* v_scale,
-                                        const int64_t* slot_mapping, int block_size, void* stream) {
+                                        const int64_t* slot_mapping, int block_size, const exl3b_kv_layout* layout,
+                                        void* stream) {
     if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads <= 0 || max_position < 1) return EXL3B_BAD_ARG;
     if (num_tokens == 0) return EXL3B_OK;
     if (!qkv || !positions || !cos_sin || !key_cache || !value_cache || !k_scale || !v_scale || !slot_mapping ||
@@ -1196,6 +1245,9 @@ extern "C" int exl3b_kv_int8_write_rope(const uint16_t* qkv, int64_t ld, uint16_
     a.key_cache = key_cache; a.value_cache = value_cache; a.k_scale = k_scale; a.v_scale = v_scale;
     a.slot_mapping = slot_mapping; a.num_tokens = (int)num_tokens; a.num_heads = num_kv_heads;
     a.block_size = block_size;
+    int al16 = 0;
+    const int lst = kv_layout(layout, block_size, num_kv_heads, kHD, key_cache, value_cache, a.lay, al16);
+    if (lst != EXL3B_OK) return lst;
     KvRopeArgs r = {};
     r.qkv = reinterpret_cast<const __half*>(qkv); r.ld = ld;
     r.q_out = reinterpret_cast<__half*>(q_out); r.ld_q = ld_q; r.nq = num_q_heads;
@@ -1220,11 +1272,11 @@ extern "C" int exl3b_kv_int4_write(const void* key, const void* value, int dtype
                                    int block_size, const float* rht_signs, const float* bias_k, const float* bias_v,
                                    const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* seq_slots,
                                    int num_seqs, uint16_t* exact_k, uint16_t* exact_v, int32_t* exact_tag,
-                                   void* stream) {
+                                   const exl3b_kv_layout* layout, void* stream) {
     KvWriteArgs a = {};
     int st = kv_write_common(a, key, value, dtype, num_tokens, num_kv_heads, head_size, k_stride_tok, k_stride_head,
                              v_stride_tok, v_stride_head, key_cache, value_cache, k_scale, v_scale, slot_mapping,
-                             block_size);
+                             block_size, layout, kHD / 2);
     if (st != EXL3B_OK || num_tokens == 0) return st;
     if (!rht_signs) return EXL3B_BAD_ARG;
     const bool exact = exact_tag != nullptr;
@@ -1256,7 +1308,7 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
                           int max_q_len, int max_seq_len, float softmax_scale, const float* rht_signs,
                           const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
                           const int32_t* seq_slots, const float* out_bias, void* workspace, size_t ws_bytes,
-                          void* stream) {
+                          const exl3b_kv_layout* layout, void* stream) {
     if (head_size != kHD || !pow2(block_size)) return EXL3B_DECLINED;
     if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return EXL3B_DECLINED;
     if (num_tokens == 0) return EXL3B_OK;
@@ -1293,6 +1345,11 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     a.partial = reinterpret_cast<float*>(ws + qr_bytes);
     a.exact_k = reinterpret_cast<const __half*>(exact_k); a.exact_v = reinterpret_cast<const __half*>(exact_v);
     a.exact_tag = exact_tag; a.seq_slots = seq_slots;
+    {
+        const int lst = kv_layout(layout, block_size, num_kv_heads, kv == 8 ? kHD : kHD / 2, key_cache, value_cache,
+                                  a.lay, a.al16);
+        if (lst != EXL3B_OK) return lst;
+    }
     const dim3 grid(num_seqs, num_kv_heads, S);
     // query rows per (sequence, KV head): up to 24 in one warp (8 per n-tile), 32 in two warps of 16
     const int rows = max_q_len * G;
@@ -1331,11 +1388,11 @@ extern "C" int exl3b_kv_int8_attn(const uint16_t* q, uint16_t* out, int num_toke
                                   int block_size, const int32_t* block_table, int64_t bt_stride,
                                   const int32_t* seq_lens, const int32_t* query_start_loc, int num_seqs,
                                   int max_q_len, int max_seq_len, float softmax_scale, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
+                                  size_t workspace_bytes, const exl3b_kv_layout* layout, void* stream) {
     return kv_attn_common(8, q, out, num_tokens, num_q_heads, num_kv_heads, head_size, key_cache, value_cache,
                           k_scale, v_scale, block_size, block_table, bt_stride, seq_lens, query_start_loc, num_seqs,
                           max_q_len, max_seq_len, softmax_scale, nullptr, nullptr, nullptr, nullptr, nullptr,
-                          nullptr, workspace, workspace_bytes, stream);
+                          nullptr, workspace, workspace_bytes, layout, stream);
 }
 
 extern "C" int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_tokens, int num_q_heads,
@@ -1346,17 +1403,17 @@ extern "C" int exl3b_kv_int4_attn(const uint16_t* q, uint16_t* out, int num_toke
                                   int max_q_len, int max_seq_len, float softmax_scale, const float* rht_signs,
                                   const uint16_t* exact_k, const uint16_t* exact_v, const int32_t* exact_tag,
                                   const int32_t* seq_slots, const float* out_bias, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
+                                  size_t workspace_bytes, const exl3b_kv_layout* layout, void* stream) {
     return kv_attn_common(4, q, out, num_tokens, num_q_heads, num_kv_heads, head_size, key_cache, value_cache,
                           k_scale, v_scale, block_size, block_table, bt_stride, seq_lens, query_start_loc, num_seqs,
                           max_q_len, max_seq_len, softmax_scale, rht_signs, exact_k, exact_v, exact_tag, seq_slots,
-                          out_bias, workspace, workspace_bytes, stream);
+                          out_bias, workspace, workspace_bytes, layout, stream);
 }
 
 static int kv_gather_common(int kv, const void* cache, const float* scale, int block_size, int num_kv_heads,
                             int head_size, const int32_t* block_ids, int64_t n, int blocks_per_seq, uint16_t* out,
                             const uint16_t* exact, const int32_t* exact_tag, const int32_t* seq_slots,
-                            const int32_t* seq_lens, void* stream) {
+                            const int32_t* seq_lens, const exl3b_kv_layout* layout, void* stream) {
     if (head_size != kHD || block_size <= 0 || num_kv_heads <= 0 || blocks_per_seq <= 0) return EXL3B_DECLINED;
     if (n < 0) return EXL3B_BAD_ARG;
     if (n == 0) return EXL3B_OK;
@@ -1368,6 +1425,9 @@ static int kv_gather_common(int kv, const void* cache, const float* scale, int b
     a.mul = kv == 4 ? 0.08838834764831845f : 1.f;
     a.exact = reinterpret_cast<const __half*>(exact); a.exact_tag = exact_tag; a.seq_slots = seq_slots;
     a.seq_lens = seq_lens;
+    int al16 = 0;
+    const int lst = kv_layout(layout, block_size, num_kv_heads, kv == 8 ? kHD : kHD / 2, cache, nullptr, a.lay, al16);
+    if (lst != EXL3B_OK) return lst;
     const int64_t items = n * block_size * num_kv_heads;
     const unsigned grid = (unsigned)((items + 7) / 8);
     if (kv == 8) kv_gather_kernel<8><<<grid, 256, 0, (cudaStream_t)stream>>>(a);
@@ -1376,15 +1436,17 @@ static int kv_gather_common(int kv, const void* cache, const float* scale, int b
 }
 
 extern "C" int exl3b_kv_int8_gather(const int8_t* cache, const float* scale, int block_size, int num_kv_heads,
-                                    int head_size, const int32_t* block_ids, int64_t n, uint16_t* out, void* stream) {
+                                    int head_size, const int32_t* block_ids, int64_t n, uint16_t* out,
+                                    const exl3b_kv_layout* layout, void* stream) {
     return kv_gather_common(8, cache, scale, block_size, num_kv_heads, head_size, block_ids, n, 1, out, nullptr,
-                            nullptr, nullptr, nullptr, stream);
+                            nullptr, nullptr, nullptr, layout, stream);
 }
 
 extern "C" int exl3b_kv_int4_gather(const uint8_t* cache, const float* scale, int block_size, int num_kv_heads,
                                     int head_size, const int32_t* block_ids, int64_t n, int blocks_per_seq,
                                     uint16_t* out, const uint16_t* exact, const int32_t* exact_tag,
-                                    const int32_t* seq_slots, const int32_t* seq_lens, void* stream) {
+                                    const int32_t* seq_slots, const int32_t* seq_lens, const exl3b_kv_layout* layout,
+                                    void* stream) {
     return kv_gather_common(4, cache, scale, block_size, num_kv_heads, head_size, block_ids, n, blocks_per_seq, out,
-                            exact, exact_tag, seq_slots, seq_lens, stream);
+                            exact, exact_tag, seq_slots, seq_lens, layout, stream);
 }

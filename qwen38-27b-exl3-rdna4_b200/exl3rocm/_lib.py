@@ -25,6 +25,12 @@ EXL3B_MAX_TP = 8
 EXL3B_IPC_HANDLE_BYTES = 72
 
 
+class KvLayout(ctypes.Structure):
+    """exl3b_kv_layout of include/exl3b.h: cache strides in bytes, scale strides in floats."""
+    _fields_ = [("cache_block", ctypes.c_int64), ("cache_slot", ctypes.c_int64), ("cache_head", ctypes.c_int64),
+                ("scale_block", ctypes.c_int64), ("scale_slot", ctypes.c_int64), ("scale_head", ctypes.c_int64)]
+
+
 class TpComm(ctypes.Structure):
     """exl3b_tp_comm of include/exl3b.h."""
     _fields_ = [("tp_size", ctypes.c_int), ("tp_rank", ctypes.c_int), ("max_blocks", ctypes.c_int),
@@ -52,11 +58,11 @@ SIGNATURES = {
     "exl3b_linear_noalloc": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp]),
     "exl3b_linear_noalloc_error": (i32, [ctypes.POINTER(i32), c_vp]),
     "exl3b_kv_int8_write": (i32, [c_vp, c_vp, i32, i64, i32, i32, i64, i64, i64, i64, c_vp, c_vp, c_vp, c_vp, c_vp,
-                                  i32, c_vp]),
+                                  i32, c_vp, c_vp]),
     "exl3b_kv_int8_write_rope": (i32, [c_vp, i64, c_vp, i64, i64, i32, i32, c_vp, c_vp, i64, c_vp, c_vp, c_vp, c_vp,
-                                       c_vp, i32, c_vp]),
+                                       c_vp, i32, c_vp, c_vp]),
     "exl3b_kv_int4_write": (i32, [c_vp, c_vp, i32, i64, i32, i32, i64, i64, i64, i64, c_vp, c_vp, c_vp, c_vp, c_vp,
-                                  i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, i32, c_vp, c_vp, c_vp, c_vp]),
+                                  i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "exl3b_tp_comm_bytes": (sz, [i32, i32, i32]),
     "exl3b_ipc_get_handle": (i32, [c_vp, c_vp]),
     "exl3b_ipc_open_handle": (i32, [c_vp, ctypes.POINTER(c_vp)]),
@@ -64,12 +70,12 @@ SIGNATURES = {
     "exl3b_linear_tp": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp, sz,
                               ctypes.POINTER(TpComm), c_vp]),
     "exl3b_kv_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
-    "exl3b_kv_int8_gather": (i32, [c_vp, c_vp, i32, i32, i32, c_vp, i64, c_vp, c_vp]),
-    "exl3b_kv_int4_gather": (i32, [c_vp, c_vp, i32, i32, i32, c_vp, i64, i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "exl3b_kv_int8_gather": (i32, [c_vp, c_vp, i32, i32, i32, c_vp, i64, c_vp, c_vp, c_vp]),
+    "exl3b_kv_int4_gather": (i32, [c_vp, c_vp, i32, i32, i32, c_vp, i64, i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "exl3b_kv_int8_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,
-                                 i32, i32, i32, f32, c_vp, sz, c_vp]),
+                                 i32, i32, i32, f32, c_vp, sz, c_vp, c_vp]),
     "exl3b_kv_int4_attn": (i32, [c_vp, c_vp, i32, i32, i32, i32, c_vp, c_vp, c_vp, c_vp, i32, c_vp, i64, c_vp, c_vp,
-                                 i32, i32, i32, f32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, sz, c_vp]),
+                                 i32, i32, i32, f32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, sz, c_vp, c_vp]),
     "exl3b_rmsnorm": (i32, [c_vp, i64, c_vp, i64, c_vp, c_vp, i64, i32, i32, f32, c_vp]),
     "exl3b_rope_neox": (i32, [c_vp, i64, c_vp, i64, i32, i32, i32, c_vp, c_vp, i64, c_vp]),
     "exl3b_silu_mul": (i32, [c_vp, i64, c_vp, i64, i32, i32, c_vp]),

@@ -170,6 +170,20 @@ def reserve_attention_workspace(device, num_tokens: int, num_q_heads: int, num_s
                                                                      num_kv_heads, max_seq_len)))
 
 
+def cache_layout(cache: torch.Tensor, scale: torch.Tensor, other: torch.Tensor | None = None,
+                 other_scale: torch.Tensor | None = None):
+    """The exl3b_kv_layout of a [blocks, block_size, heads, row] cache view and its [blocks, block_size,
+    heads] fp32 scale view, any strides with a unit last cache stride: dense caches and vLLM's
+    per-token-head caches (scales inline, K and V interleaved per block) alike.  `other` / `other_scale`
+    (the V side) must share the strides."""
+    assert cache.dim() == 4 and cache.stride(-1) == 1 and scale.dim() == 3 and scale.dtype == torch.float32
+    if other is not None:
+        assert other.stride() == cache.stride() and other_scale.stride() == scale.stride(), "K and V layouts differ"
+    e = cache.element_size()
+    return _lib.ctypes.byref(_lib.KvLayout(cache.stride(0) * e, cache.stride(1) * e, cache.stride(2) * e,
+                                           scale.stride(0), scale.stride(1), scale.stride(2)))
+
+
 def _dtype_code(t: torch.Tensor) -> int:
     if t.dtype == torch.float16:
         return 0
@@ -192,12 +206,12 @@ def reshape_and_cache_int8(key, value, key_cache, value_cache, slot_mapping, k_s
     n = min(key.shape[0], slot_mapping.shape[0])
     if n == 0:
         return
-    assert key_cache.is_contiguous() and value_cache.is_contiguous() and k_scale_cache.is_contiguous()
+    lay = cache_layout(key_cache, k_scale_cache, value_cache, v_scale_cache)
     slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
     _lib.call("exl3b_kv_int8_write", key.data_ptr(), value.data_ptr(), _dtype_code(key), n, key.shape[1],
               HEAD_SIZE, key.stride(0), key.stride(1), value.stride(0), value.stride(1), key_cache.data_ptr(),
               value_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(), slots.data_ptr(),
-              key_cache.shape[1], _stream(key.device))
+              key_cache.shape[1], lay, _stream(key.device))
 
 
 def rope_and_cache_int8(qkv, q_out, num_q_heads, num_kv_heads, positions, cos_sin, key_cache, value_cache,
@@ -210,12 +224,12 @@ def rope_and_cache_int8(qkv, q_out, num_q_heads, num_kv_heads, positions, cos_si
     n = min(qkv.shape[0], slot_mapping.shape[0])
     if n == 0:
         return
-    assert key_cache.is_contiguous() and value_cache.is_contiguous() and k_scale_cache.is_contiguous()
+    lay = cache_layout(key_cache, k_scale_cache, value_cache, v_scale_cache)
     slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
     _lib.call("exl3b_kv_int8_write_rope", qkv.data_ptr(), qkv.stride(0), q_out.data_ptr(), q_out.stride(0), n,
               num_q_heads, num_kv_heads, positions.data_ptr(), cos_sin.data_ptr(), cos_sin.shape[0],
               key_cache.data_ptr(), value_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(),
-              slots.data_ptr(), key_cache.shape[1], _stream(qkv.device))
+              slots.data_ptr(), key_cache.shape[1], lay, _stream(qkv.device))
 
 
 def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, *, k_scale_cache, v_scale_cache,
@@ -235,6 +249,7 @@ def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, *, k_sca
     qsl = query_start_loc.to(torch.int32) if use_ex and query_start_loc.dtype != torch.int32 else query_start_loc
     sl = seq_lens.to(torch.int32) if use_ex and seq_lens.dtype != torch.int32 else seq_lens
     bias = layer_bias(layer_name, heads, key.device)
+    lay = cache_layout(key_cache, k_scale_cache, value_cache, v_scale_cache)
     _lib.call("exl3b_kv_int4_write", key.data_ptr(), value.data_ptr(), _dtype_code(key), n, heads, HEAD_SIZE,
               key.stride(0), key.stride(1), value.stride(0), value.stride(1), key_cache.data_ptr(),
               value_cache.data_ptr(), k_scale_cache.data_ptr(), v_scale_cache.data_ptr(), slots.data_ptr(),
@@ -243,20 +258,22 @@ def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, *, k_sca
               qsl.data_ptr() if use_ex else None, sl.data_ptr() if use_ex else None,
               _req["slot"].data_ptr() if use_ex else None, num_seqs,
               ex["k"].data_ptr() if use_ex else None, ex["v"].data_ptr() if use_ex else None,
-              ex["tag"].data_ptr() if use_ex else None, _stream(key.device))
+              ex["tag"].data_ptr() if use_ex else None, lay, _stream(key.device))
 
 
 # ---------------------------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------------------------
-def supported(kw) -> bool:
-    """Features the kernels leave out (kv_int4.py:499-504): the caller falls back otherwise."""
+def supported(kw, prefill: bool = False) -> bool:
+    """Features the kernels leave out (kv_int4.py:499-504): the caller falls back otherwise.  The
+    split-KV decode / verify kernels also take at most MAX_ROWS query rows per sequence and KV head;
+    the prefill route (prefill=True: gather, then an fp16 kernel) takes any query length."""
     q = kw["q"]
     return (kw.get("alibi_slopes") is None and kw.get("sinks") is None and not kw.get("softcap")
             and kw.get("qq_bias") is None and kw.get("mm_prefix_range") is None and kw.get("output_scale") is None
             and tuple(kw.get("window_size", (-1, -1)))[0] < 0 and kw.get("causal", True) is True
             and q.dtype == torch.float16 and q.shape[-1] == HEAD_SIZE
-            and int(kw.get("max_seqlen_q", 1)) * (q.shape[1] // kw["k"].shape[2]) <= MAX_ROWS)
+            and (prefill or int(kw.get("max_seqlen_q", 1)) * (q.shape[1] // kw["k"].shape[2]) <= MAX_ROWS))
 
 
 def _attn(kind, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale,
@@ -264,6 +281,7 @@ def _attn(kind, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table
     T, hq, d = q.shape
     hkv = k.shape[2]
     assert d == HEAD_SIZE and q.is_contiguous() and out.is_contiguous() and q.dtype == torch.float16
+    lay = cache_layout(k, k_scale_cache, v, v_scale_cache)
     num_seqs = seqused_k.shape[0]
     max_k = int(max_seqlen_k) if max_seqlen_k is not None else int(block_table.shape[1] * k.shape[1])
     nbytes = int(_lib.lib().exl3b_kv_attn_workspace_bytes(T, hq, num_seqs, hkv, max_k))
@@ -275,7 +293,7 @@ def _attn(kind, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table
               v_scale_cache.data_ptr(), k.shape[1], bt.data_ptr(), bt.stride(0), sl.data_ptr(), qsl.data_ptr(),
               num_seqs, int(max_seqlen_q), max_k, float(softmax_scale))
     if kind == 8:
-        _lib.call("exl3b_kv_int8_attn", *common, ws.data_ptr(), ws.numel(), _stream(q.device))
+        _lib.call("exl3b_kv_int8_attn", *common, ws.data_ptr(), ws.numel(), lay, _stream(q.device))
         return
     ex = _exact.get(layer_name) if layer_name else None
     use_ex = ex is not None and _req["slot"] is not None
@@ -283,7 +301,7 @@ def _attn(kind, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table
     _lib.call("exl3b_kv_int4_attn", *common, rht_signs(q.device).data_ptr(),
               ex["k"].data_ptr() if use_ex else None, ex["v"].data_ptr() if use_ex else None,
               ex["tag"].data_ptr() if use_ex else None, _req["slot"].data_ptr() if use_ex else None,
-              bias["v_mean"].data_ptr() if bias else None, ws.data_ptr(), ws.numel(), _stream(q.device))
+              bias["v_mean"].data_ptr() if bias else None, ws.data_ptr(), ws.numel(), lay, _stream(q.device))
 
 
 def attention(*, q, k, v, out, cu_seqlens_q, max_seqlen_q, seqused_k, block_table, softmax_scale,
@@ -326,7 +344,7 @@ def gather_dequant_int8(cache, scale, blocks, tag="k"):
     ids = blocks.to(torch.int32).contiguous()
     out = _gather_buffer(tag, cache.device, ids.numel(), bs, heads)
     _lib.call("exl3b_kv_int8_gather", cache.data_ptr(), scale.data_ptr(), bs, heads, HEAD_SIZE, ids.data_ptr(),
-              ids.numel(), out.data_ptr(), _stream(cache.device))
+              ids.numel(), out.data_ptr(), cache_layout(cache, scale), _stream(cache.device))
     return out
 
 
@@ -342,7 +360,7 @@ def gather_dequant_int4(cache, scale, blocks, nb, tag="k", exact=None, seq_lens=
     _lib.call("exl3b_kv_int4_gather", cache.data_ptr(), scale.data_ptr(), bs, heads, HEAD_SIZE, ids.data_ptr(),
               ids.numel(), nb, out.data_ptr(), exact[0].data_ptr() if use_ex else None,
               exact[1].data_ptr() if use_ex else None, _req["slot"].data_ptr() if use_ex else None,
-              sl.data_ptr() if use_ex else None, _stream(cache.device))
+              sl.data_ptr() if use_ex else None, cache_layout(cache, scale), _stream(cache.device))
     return out
 
 

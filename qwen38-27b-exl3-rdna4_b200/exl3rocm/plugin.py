@@ -1,5 +1,5 @@
 """vLLM out-of-tree quantization plugin "exl3" for B200: the reference's plugin surface
-(``vllm_plugin/exl3rocm/plugin.py``), with tensor-parallel weights.
+(``vllm_plugin/exl3rocm/plugin.py``), with tensor-parallel weights and this library's KV kernels.
 
 Registered through the ``vllm.general_plugins`` entry point ``exl3rocm = exl3rocm.plugin:register``
 (reference ``vllm_plugin/pyproject.toml:13-14``).  What it keeps from the reference's behaviour:
@@ -9,7 +9,9 @@ Registered through the ``vllm.general_plugins`` entry point ``exl3rocm = exl3roc
   (``plugin.py:63-79``);
 * fused vLLM modules (qkv_proj, gate_up_proj, ...) hold one group per checkpoint tensor, each with
   its own K, trellis, suh and svh, and run as one ``exl3rocm::linear_groups`` op
-  (``plugin.py:236-372``).
+  (``plugin.py:236-372``);
+* the per-token-head KV caches are routed to this library's write / attention / prefill kernels
+  through the Triton attention backend's hook points (``plugin.py:586-740``; see ``KvRouting``).
 
 What differs: ``create_weights`` accepts tensor-parallel partitions (the reference raises,
 ``plugin.py:255-257``).  Each rank stores only its shard (``exl3rocm.sharding``): column-parallel
@@ -44,6 +46,7 @@ FUSED = {
     "qkv": ["q_proj", "k_proj", "v_proj"],
 }
 SHARD_IDS = {"q": 0, "k": 1, "v": 2}
+CODEBOOK_SCALARS = ("mul1", "mcg")  # the scalar tensor a checkpoint stores names its codebook
 
 
 def module_key(name: str) -> str:
@@ -91,7 +94,8 @@ def _tp_group():
 
 @register_quantization_config("exl3")
 class Exl3Config(QuantizationConfig):
-    """Quant config "exl3"; the module map is filled from the checkpoint by maybe_update_config."""
+    """Quant config "exl3".  ``modules`` maps checkpoint module keys to (K, k, n); vLLM fills it
+    through maybe_update_config with the checkpoint directory."""
 
     def __init__(self, codebook: str = "mul1"):
         super().__init__()
@@ -99,7 +103,8 @@ class Exl3Config(QuantizationConfig):
         self.modules: dict[str, tuple[int, int, int]] = {}
 
     def __repr__(self):
-        return f"Exl3Config(codebook={self.codebook}, modules={len(self.modules)})"
+        widths = sorted({K for K, _, _ in self.modules.values()})
+        return f"exl3[{self.codebook}, {len(self.modules)} EXL3 modules, K in {widths}]"
 
     def get_name(self):
         return "exl3"
@@ -120,30 +125,36 @@ class Exl3Config(QuantizationConfig):
         return cls(codebook=config.get("codebook", "mul1"))
 
     def maybe_update_config(self, model_name: str, hf_config=None, revision=None):
+        # the module map is read from the checkpoint's own files: a hub id has none yet
         if not os.path.isdir(model_name):
-            raise NotImplementedError("exl3rocm: pass a local checkpoint directory")
+            raise NotImplementedError(f"exl3: {model_name!r} is not a directory; the EXL3 module map is read "
+                                      "from the checkpoint's safetensors headers")
         self.modules = read_checkpoint_layout(model_name)
 
     def groups_for(self, prefix: str) -> Optional[list[tuple[str, int, int, int]]]:
-        """The checkpoint members of the (possibly fused) vLLM module at ``prefix`` as
-        [(member, K, k, n)], or None when the module is not EXL3."""
+        """[(member, K, k, n)] for the checkpoint tensors behind the (possibly fused) vLLM module at
+        ``prefix``; None when none of them is EXL3; ValueError when only some are."""
         key = module_key(prefix)
-        base, _, leaf = key.rpartition(".")
-        members = [f"{base}.{p}" if base else p for p in FUSED.get(leaf, [leaf])]
-        found = [self.modules.get(m) for m in members]
-        if all(f is None for f in found):
+        parent, _, leaf = key.rpartition(".")
+        qualify = (lambda m: f"{parent}.{m}") if parent else (lambda m: m)
+        members = [qualify(m) for m in FUSED.get(leaf, [leaf])]
+        shapes = {m: self.modules[m] for m in members if m in self.modules}
+        if not shapes:
             return None
-        if any(f is None for f in found):
-            raise ValueError(f"exl3rocm: partially quantized fused module {prefix}")
-        return [(m, *f) for m, f in zip(members, found)]
+        if len(shapes) != len(members):
+            missing = [m for m in members if m not in shapes]
+            raise ValueError(f"exl3: fused module {prefix} is only partly EXL3 (no trellis for {missing})")
+        return [(m, *shapes[m]) for m in members]
 
     def get_quant_method(self, layer: torch.nn.Module, prefix: str):
-        if isinstance(layer, (LinearBase, ParallelLMHead)):
-            groups = self.groups_for(prefix)
-            if groups is None:
-                return UnquantizedLinearMethod() if isinstance(layer, LinearBase) else None
+        is_linear = isinstance(layer, LinearBase)
+        if not (is_linear or isinstance(layer, ParallelLMHead)):
+            return None
+        groups = self.groups_for(prefix)
+        if groups is not None:
             return Exl3LinearMethod(self, groups)
-        return None
+        # a plain (unquantised) linear keeps vLLM's method; an lm_head keeps vLLM's default
+        return UnquantizedLinearMethod() if is_linear else None
 
 
 def parallel_mode(input_size_per_partition: int, input_size: int, output_partition_sizes: list[int],
@@ -153,6 +164,39 @@ def parallel_mode(input_size_per_partition: int, input_size: int, output_partiti
     if sum(output_partition_sizes) != output_size:
         return "column"
     return "replicated"
+
+
+class _ShardLoader:
+    """weight_loader of one registered load target: hands each full checkpoint tensor to this
+    rank's shard of the group the vLLM shard id names (or records the codebook scalar)."""
+
+    def __init__(self, layer, kind: str):
+        self.layer, self.kind = layer, kind
+
+    def group(self, shard_id) -> int:
+        owner = self.layer.exl3_part_to_group
+        if shard_id is None:
+            if len(self.layer.exl3_shard.groups) > 1:
+                raise ValueError("exl3: a fused module got a tensor without a shard id")
+            return 0
+        if isinstance(shard_id, str):
+            parts = (SHARD_IDS[shard_id],)
+        elif isinstance(shard_id, int):
+            parts = (shard_id,)
+        else:
+            parts = tuple(shard_id)
+        owners = sorted({owner[p] for p in parts})
+        if len(owners) > 1:
+            raise ValueError(f"exl3: shard id {shard_id} covers groups {owners} of one module")
+        return owners[0]
+
+    def __call__(self, param, loaded: torch.Tensor, shard_id=None, *args, **kwargs):
+        if self.kind in CODEBOOK_SCALARS:
+            seen = self.layer.exl3_codebook.setdefault(self.kind, int(loaded.item()))
+            if seen != int(loaded.item()):
+                raise ValueError(f"exl3: the groups of one module disagree on {self.kind}")
+            return
+        self.layer.exl3_shard.load(self.kind, self.group(shard_id), loaded)
 
 
 class Exl3LinearMethod(LinearMethodBase):
@@ -168,63 +212,24 @@ class Exl3LinearMethod(LinearMethodBase):
     def create_weights(self, layer, input_size_per_partition, output_partition_sizes, input_size, output_size,
                        params_dtype, **extra_weight_attrs):
         tp_size, tp_rank = self.tp or _tp()
-        mode = parallel_mode(input_size_per_partition, input_size, list(output_partition_sizes), output_size)
+        partitions = [int(p) for p in output_partition_sizes]
+        mode = parallel_mode(input_size_per_partition, input_size, partitions, output_size)
         shard = sharding.module_shard(self.groups, mode, tp_size, tp_rank,
                                       device=torch.cuda.current_device() if torch.cuda.is_available() else "cpu")
         if mode == "row" and shard.local_k != input_size_per_partition:
-            raise ValueError(f"exl3rocm: row shard k={shard.local_k}, vLLM expects {input_size_per_partition}")
-        # map vLLM's output partitions onto groups (a group may span partitions, e.g. q, k, v of
-        # in_proj_qkv inside in_proj_qkvz)
-        widths, part_to_group, gi, acc = shard.out_sizes, [], 0, 0
-        for p in output_partition_sizes:
-            if gi >= len(widths):
-                raise ValueError(f"exl3rocm: partitions {list(output_partition_sizes)} do not tile groups {widths}")
-            part_to_group.append(gi)
-            acc += p
-            if acc > widths[gi]:
-                raise ValueError(f"exl3rocm: partitions {list(output_partition_sizes)} do not tile groups {widths}")
-            if acc == widths[gi]:
-                gi, acc = gi + 1, 0
-        if gi != len(widths):
-            raise ValueError(f"exl3rocm: partitions {list(output_partition_sizes)} do not tile groups {widths}")
+            raise ValueError(f"exl3: this rank's input slice has {shard.local_k} features, "
+                             f"vLLM expects {input_size_per_partition}")
         layer.exl3_shard = shard
-        layer.exl3_part_to_group = part_to_group
+        layer.exl3_part_to_group = sharding.partition_owners(partitions, shard.out_sizes)
         layer.exl3_codebook = {}
-
-        def reg(name, loader):
-            p = Parameter(torch.empty(0, dtype=torch.int8), requires_grad=False)
-            p.weight_loader = loader
-            layer.register_parameter(name, p)
-
-        for kind in ("trellis", "suh", "svh"):
-            reg(kind, self._loader(layer, kind))
-        if self.config.codebook in ("mul1", "mcg"):
-            reg(self.config.codebook, self._loader(layer, self.config.codebook))
-
-    @staticmethod
-    def _group_of(layer, shard_id) -> int:
-        if shard_id is None:
-            if len(layer.exl3_shard.groups) != 1:
-                raise ValueError("exl3rocm: unsharded load into a fused module")
-            return 0
-        parts = [SHARD_IDS[shard_id]] if isinstance(shard_id, str) else (
-            [shard_id] if isinstance(shard_id, int) else list(shard_id))
-        gs = {layer.exl3_part_to_group[p] for p in parts}
-        if len(gs) != 1:
-            raise ValueError(f"exl3rocm: shard {shard_id} spans groups {gs}")
-        return gs.pop()
-
-    def _loader(self, layer, kind):
-        def load(param, loaded, shard_id=None, *args, **kwargs):
-            if kind in ("mul1", "mcg"):  # one codebook for the whole module: no group needed
-                val = int(loaded.item())
-                prev = layer.exl3_codebook.get(kind)
-                if prev is not None and prev != val:
-                    raise ValueError(f"exl3rocm: {kind} differs across groups")
-                layer.exl3_codebook[kind] = val
-                return
-            layer.exl3_shard.load(kind, self._group_of(layer, shard_id), loaded)
-        return load
+        targets = ["trellis", "suh", "svh"]
+        if self.config.codebook in CODEBOOK_SCALARS:  # only what the checkpoint stores is registered
+            targets.append(self.config.codebook)
+        layer.exl3_load_targets = tuple(targets)
+        for kind in targets:
+            target = Parameter(torch.empty(0, dtype=torch.int8), requires_grad=False)
+            target.weight_loader = _ShardLoader(layer, kind)
+            layer.register_parameter(kind, target)
 
     def process_weights_after_loading(self, layer):
         shard = layer.exl3_shard
@@ -232,68 +237,195 @@ class Exl3LinearMethod(LinearMethodBase):
         layer.exl3_mul1 = "mul1" in layer.exl3_codebook
         layer.exl3_mcg = "mcg" in layer.exl3_codebook
         if torch.cuda.is_available():
-            from .ops import GEMV_MAX_ROWS, RECON_SLICE_N, reserve_weight_buffer, reserve_workspace
-            dev = shard.shards[0].trellis.device
+            from .ops import GEMV_MAX_ROWS, reserve_workspace
             stored = [s.stored_n for s in shard.shards]
-            reserve_workspace(dev, shard.local_k, sum(stored), len(stored), GEMV_MAX_ROWS)
-            reserve_weight_buffer(dev, shard.local_k * min(max(stored), RECON_SLICE_N))
-        for name in ("trellis", "suh", "svh", "mul1", "mcg"):
-            if name in layer._parameters:
-                del layer._parameters[name]
+            reserve_workspace(shard.shards[0].trellis.device, shard.local_k, sum(stored), len(stored), GEMV_MAX_ROWS)
+        # the load targets have served their purpose; weights live in the shard
+        for kind in layer.exl3_load_targets:
+            layer._parameters.pop(kind, None)
 
     def apply(self, layer, x, bias=None):
         y = layer.exl3_shard.forward(x, layer.exl3_mcg, layer.exl3_mul1)
-        if y.dtype != x.dtype:
-            y = y.to(x.dtype)
-        if bias is not None:
-            y = y + bias
-        return y
+        y = y if y.dtype == x.dtype else y.to(x.dtype)
+        return y if bias is None else y + bias
 
     def embedding(self, layer, input_):
-        raise NotImplementedError("exl3rocm: quantized input embeddings are not supported")
+        raise NotImplementedError("exl3: this plugin quantises linears only; the input embedding stays dense")
+
+
+# ---------------------------------------------------------------------------------------------
+# KV cache routing (reference plugin.py:586-740)
+# ---------------------------------------------------------------------------------------------
+class KvRouting:
+    """Sends vLLM's per-token-head KV cache traffic on the Triton attention backend to exl3rocm.kv.
+
+    * cache write (``TritonAttentionImpl.do_kv_cache_update``): int8 -> ``kv.reshape_and_cache_int8``;
+      int4 -> ``kv.reshape_and_cache`` with the batch's query_start_loc / seq_lens taken from vLLM's
+      per-layer attention context (they locate each request's newest positions for the exact rows);
+    * attention (the backend module's ``unified_attention``): decode / speculative verify to
+      ``kv.attention_int8`` / ``kv.attention``; prefill chunks of at least ``prefill_min_q`` query
+      tokens outside graph capture to ``kv.prefill_int8`` / ``kv.prefill`` (the sequences' blocks
+      dequantised once to fp16, then vLLM's own fp16 kernel); calls the kernels do not implement
+      (``kv.supported``: ALiBi, sinks, softcap, sliding window, non-fp16 q, ...) stay with vLLM;
+    * ``TritonAttentionImpl.forward`` records the running layer's name for the duration of the call
+      (the int4 exact rows and the centering means are per layer);
+    * request slots (the V2 model runner's ``RequestState``): the slot count at construction, a slot's
+      exact rows cleared when a new request takes it, and the batch's row -> slot map before each
+      forward (``kv.configure_request_slots`` / ``request_added`` / ``set_batch_slots``).
+
+    vLLM's caches keep each row's fp32 scale inline after it; the kernels get the cache and scale
+    views' strides (``kv.cache_layout``), so no cache is copied."""
+
+    def __init__(self, ta, modes, kv, get_context=None):
+        self.ta, self.kv, self.get_context = ta, kv, get_context
+        self.int8 = modes.get("int8")
+        self.int4 = modes.get("int4")
+        self.none = modes.get("none")
+        self.prefill_min_q = int(os.environ.get("EXL3_PTH_PREFILL_MIN_Q", "32"))
+        self.layer: Optional[str] = None
+        self.descale: dict = {}
+
+    def _ours(self, mode) -> bool:
+        return mode is not None and mode in (self.int8, self.int4)
+
+    @staticmethod
+    def _rows(cache: torch.Tensor, row_bytes: int) -> torch.Tensor:
+        """The [blocks, block_size, heads, row bytes] view of a vLLM cache half (inline scale cut off)."""
+        return cache[..., :row_bytes] if cache.shape[-1] > row_bytes else cache
+
+    def _metadata(self, layer_name):
+        if not layer_name or self.get_context is None:
+            return None
+        try:
+            return self.get_context(layer_name)[0]
+        except Exception:
+            return None
+
+    # -- hooks ------------------------------------------------------------------------------------
+    def kv_update(self, orig, impl, layer, key, value, kv_cache, slot_mapping):
+        mode = getattr(impl, "_kv_quant_mode", None)
+        decoder = getattr(getattr(impl, "attn_type", None), "name", "DECODER") in ("DECODER", "ENCODER_DECODER")
+        if not (self._ours(mode) and decoder and key.dtype in (torch.float16, torch.bfloat16)
+                and key.shape[-1] == self.kv.HEAD_SIZE):
+            return orig(impl, layer, key, value, kv_cache, slot_mapping)
+        impl._ensure_scale_caches(kv_cache)
+        kc, vc = kv_cache.unbind(1)
+        name = getattr(layer, "layer_name", None)
+        if mode == self.int8:
+            self.kv.reshape_and_cache_int8(key, value, self._rows(kc, 128), self._rows(vc, 128),
+                                           slot_mapping, impl._k_scale_cache, impl._v_scale_cache)
+            return None
+        md = self._metadata(name)
+        self.kv.reshape_and_cache(key, value, self._rows(kc, 64), self._rows(vc, 64), slot_mapping,
+                                  k_scale_cache=impl._k_scale_cache, v_scale_cache=impl._v_scale_cache,
+                                  layer_name=name, query_start_loc=getattr(md, "query_start_loc", None),
+                                  seq_lens=getattr(md, "seq_lens", None))
+        return None
+
+    def attention(self, orig, *args, **kw):
+        mode = kw.get("kv_quant_mode")
+        if args or not self._ours(mode):
+            return orig(*args, **kw)
+        capturing = torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+        long_prefill = int(kw.get("max_seqlen_q", 1)) >= self.prefill_min_q and not capturing
+        if not self.kv.supported(kw, prefill=long_prefill):
+            return orig(*args, **kw)
+        row = 128 if mode == self.int8 else 64
+        kw = dict(kw, k=self._rows(kw["k"], row), v=self._rows(kw["v"], row))
+        if long_prefill:
+            dense = self._dense_kwargs(kw)
+            if mode == self.int8:
+                return self.kv.prefill_int8(orig, dense)
+            return self.kv.prefill(orig, dense, layer_name=self.layer)
+        if mode == self.int8:
+            return self.kv.attention_int8(**kw)
+        return self.kv.attention(**kw, layer_name=self.layer)
+
+    def _dense_kwargs(self, kw) -> dict:
+        """vLLM's unified_attention arguments for the fp16 cache the prefill gathers: no quant mode,
+        unit descales (one per sequence and KV head, as vLLM passes for an unquantised cache)."""
+        seqs, heads = kw["block_table"].shape[0], kw["k"].shape[2]
+        key = (kw["q"].device, heads)
+        if key not in self.descale:
+            self.descale[key] = torch.ones((1, 1), dtype=torch.float32, device=kw["q"].device)
+        unit = self.descale[key].expand(seqs, heads)
+        return dict(kw, kv_quant_mode=self.none, k_descale=unit, v_descale=unit)
+
+    def forward(self, orig, impl, layer, *args, **kw):
+        outer, self.layer = self.layer, getattr(layer, "layer_name", None)
+        try:
+            return orig(impl, layer, *args, **kw)
+        finally:
+            self.layer = outer
+
+    # -- installation -------------------------------------------------------------------------------
+    def install(self) -> None:
+        ta, cls = self.ta, self.ta.TritonAttentionImpl
+        inner_attention, inner_update, inner_forward = ta.unified_attention, cls.do_kv_cache_update, cls.forward
+        ta.unified_attention = lambda *a, **kw: self.attention(inner_attention, *a, **kw)
+        cls.do_kv_cache_update = lambda impl, layer, k, v, cache, slots: self.kv_update(
+            inner_update, impl, layer, k, v, cache, slots)
+        cls.forward = lambda impl, layer, *a, **kw: self.forward(inner_forward, impl, layer, *a, **kw)
+        ta._exl3_kv_routing = self
+
+    def install_request_slots(self, states, runner) -> bool:
+        """Feed the exact-row ring from the V2 model runner (None when that runner is absent)."""
+        if states is None or runner is None or getattr(states.RequestState, "_exl3_slots", False):
+            return False
+        kv, rs_cls, mr_cls = self.kv, states.RequestState, runner.GPUModelRunner
+        init, add, prep = rs_cls.__init__, rs_cls.add_request, mr_cls.prepare_inputs
+
+        def state_init(st, *a, **k):
+            init(st, *a, **k)
+            kv.configure_request_slots(st.max_num_reqs)
+
+        def state_add(st, req_id, *a, **k):
+            add(st, req_id, *a, **k)
+            kv.request_added(st.req_id_to_index[req_id])
+
+        def prepare(runner_self, *a, **k):
+            batch = prep(runner_self, *a, **k)
+            kv.set_batch_slots(batch.idx_mapping)
+            return batch
+
+        rs_cls.__init__, rs_cls.add_request, mr_cls.prepare_inputs = state_init, state_add, prepare
+        rs_cls._exl3_slots = True
+        return True
 
 
 def _install_kv_hooks():
-    """Route vLLM's int4_per_token_head cache write and decode attention to exl3rocm.kv, where the
-    running vLLM has the hook points the reference patches (``plugin.py:639-740``: the triton
-    attention backend's ``unified_attention`` and ``do_kv_cache_update``, the V2 runner's request
-    states).  Silently absent otherwise (vLLM 0.22 has no int4_per_token_head)."""
+    """Install KvRouting on the running vLLM (once).  int8_per_token_head routes on any vLLM that has
+    the mode (0.22 here); int4_per_token_head where vLLM defines it (0.28, the reference's).  Returns
+    the routing object, or None when the Triton backend or the quant modes are missing."""
     try:
         from vllm.v1.attention.backends import triton_attn as ta
         from vllm.v1.kv_cache_interface import KVQuantMode
     except Exception:
-        return False
-    if getattr(ta, "_exl3_kv_int4", False):
-        return True
+        return None
+    if getattr(ta, "_exl3_kv_routing", None) is not None:
+        return ta._exl3_kv_routing
+    modes = {"int8": getattr(KVQuantMode, "INT8_PER_TOKEN_HEAD", None),
+             "int4": getattr(KVQuantMode, "INT4_PER_TOKEN_HEAD", None), "none": KVQuantMode.NONE}
+    if modes["int8"] is None and modes["int4"] is None:
+        return None
+    try:
+        from vllm.model_executor.layers.attention.attention import get_attention_context
+    except Exception:
+        get_attention_context = None
     from . import kv
-    int4 = KVQuantMode.INT4_PER_TOKEN_HEAD
-    inner = ta.unified_attention
-
-    def unified_attention(*args, **kw):
-        if args or kw.get("kv_quant_mode") != int4 or not kv.supported(kw):
-            return inner(*args, **kw)
-        return kv.attention(**kw)
-
-    ta.unified_attention = unified_attention
-    cls = ta.TritonAttentionImpl
-    orig_update = cls.do_kv_cache_update
-
-    def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping):
-        if getattr(self, "_kv_quant_mode", None) != int4:
-            return orig_update(self, layer, key, value, kv_cache, slot_mapping)
-        key_cache, value_cache = self._pth_key_value_caches(kv_cache)
-        kv.reshape_and_cache(key, value, key_cache, value_cache, slot_mapping,
-                             k_scale_cache=self._k_scale_cache, v_scale_cache=self._v_scale_cache,
-                             layer_name=getattr(layer, "layer_name", None))
-
-    cls.do_kv_cache_update = do_kv_cache_update
-    ta._exl3_kv_int4 = True
-    return True
+    routing = KvRouting(ta, modes, kv, get_attention_context)
+    routing.install()
+    try:
+        from vllm.v1.worker.gpu import model_runner, states
+    except Exception:
+        model_runner = states = None
+    routing.install_request_slots(states, model_runner)
+    return routing
 
 
 def register():
     """vllm.general_plugins entry point (runs in every vLLM process)."""
     from . import ops  # noqa: F401  registers torch.ops.exl3rocm.*
-    if os.environ.get("EXL3_KV_INT4", "1") != "0":
+    if os.environ.get("EXL3_KV_ROUTING", "1") != "0":
         _install_kv_hooks()
     return None

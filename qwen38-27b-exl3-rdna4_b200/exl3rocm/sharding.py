@@ -21,6 +21,9 @@ The split is contiguous and balanced: rank ``r`` of ``tp`` owns ``[r * size / tp
 """
 from __future__ import annotations
 
+import bisect
+import itertools
+
 from dataclasses import dataclass, field
 from typing import Optional, Sequence
 
@@ -198,6 +201,25 @@ class ModuleShard:
         tr, su, sv, Ks = self.tensors()
         y = torch.ops.exl3rocm.linear_groups(self.local_x(x), tr, su, sv, Ks, mcg, mul1)
         return self.trim(y)
+
+
+def partition_owners(partitions: Sequence[int], widths: Sequence[int]) -> list[int]:
+    """The group each of vLLM's output partitions falls in, given the groups' output widths on this rank.
+    Partitions must tile the groups in order, several partitions may share one group (q, k and v of
+    in_proj_qkv inside in_proj_qkvz), and none may straddle two."""
+    ends = list(itertools.accumulate(widths))
+    owners, start = [], 0
+    for p in partitions:
+        g = bisect.bisect_right(ends, start)
+        if p <= 0 or g >= len(ends) or start + p > ends[g]:
+            raise ValueError(f"exl3: vLLM output partitions {list(partitions)} do not tile the module's groups "
+                             f"{list(widths)}")
+        owners.append(g)
+        start += p
+    if start != (ends[-1] if ends else 0):
+        raise ValueError(f"exl3: vLLM output partitions {list(partitions)} cover {start} of the groups' "
+                         f"{ends[-1] if ends else 0} columns")
+    return owners
 
 
 def agree_loaded(shards: Sequence[ModuleShard], group=None) -> None:

@@ -100,7 +100,7 @@ def _int4_write_via_abi(g, layer):
               key.stride(1), val.stride(0), val.stride(1), kc.data_ptr(), vc.data_ptr(), ks.data_ptr(), vs.data_ptr(),
               slots.data_ptr(), BS, signs.data_ptr(), bk.data_ptr() if bk is not None else None,
               bv.data_ptr() if bv is not None else None, qsl.data_ptr(), slt.data_ptr(), seq_slots.data_ptr(),
-              len(sl), exk.data_ptr(), exv.data_ptr(), tag.data_ptr(), _stream())
+              len(sl), exk.data_ptr(), exv.data_ptr(), tag.data_ptr(), None, _stream())
     torch.cuda.synchronize()
     return kc, vc, ks, vs, exk, exv, tag, seq_slots
 
@@ -135,7 +135,7 @@ def test_int4_attention_matches_reference_fixture(g, layer, name, qkey, qsl):
               ksr.data_ptr(), vsr.data_ptr(), BS, bt.data_ptr(), bt.stride(0), sl.data_ptr(), qs.data_ptr(), 2,
               int(np.diff(qsl).max()), int(g["seq_lens"].max()), D ** -0.5, t(g["signs"]).data_ptr(), exk.data_ptr(),
               exv.data_ptr(), tag.data_ptr(), seq_slots.data_ptr(), vmean.data_ptr() if vmean is not None else None,
-              ws.data_ptr(), ws.numel(), _stream())
+              ws.data_ptr(), ws.numel(), None, _stream())
     torch.cuda.synchronize()
     check_attention(out.cpu().numpy(), g[p + f"out_{name}"].astype(np.float64))
 
