@@ -479,6 +479,144 @@ def bench_decode(torch, dev, steps: int, warmup: int, ctx: int = 32768,
     return out
 
 
+def bench_c5(torch, dev, world: int, rank: int, pg, comm=None, iters: int = 3) -> dict:
+    """The tensor-parallel workloads: batch-64 decode with an int4 KV cache of 64k tokens per sequence
+    (64 layers: 285 GB of cache in all, so from 2 GPUs on), and an 8192-token prefill of one prompt
+    into an int4 cache (GEMM linears, the cache write, prefill attention).  Eager steps, event-timed,
+    max over ranks."""
+    from exl3rocm.synthetic import DecoderShape, SyntheticDecoder
+    shape = DecoderShape()
+    out = {}
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier(device_ids=[dev.index])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=pg)
+            ms = float(t.item())
+        return ms
+
+    # prefill: one 8192-token prompt
+    dec = None
+    try:
+        dec = SyntheticDecoder(shape, dev, batch=1, q_len=1, ctx=8192, seed=2024, tp_size=world, tp_rank=rank,
+                               comm=comm, group=pg, kv_cache="int4")
+        g = torch.Generator(device=dev)
+        g.manual_seed(8192)
+        prompt = torch.randint(0, shape.vocab, (8192,), generator=g, device=dev)
+        ms = timed(lambda: dec.prefill(prompt))
+        h, d, it = shape.hidden, shape.head, shape.intermediate
+        weights = h * (shape.q_heads + 2 * shape.kv_heads) * d + shape.q_heads * d * h + 3 * h * it
+        fl = 2.0 * 8192 * shape.layers * weights  # 2 M k n over one layer's linears, all layers
+        out["prefill_8192_int4"] = {"tokens": 8192, "ms": ms, "tok_s": 8192 / (ms * 1e-3), "tp": world,
+                                    "linear_tflops": fl / (ms * 1e-3) / 1e12,
+                                    "note": "eager; includes RMSNorm, RoPE, the int4 cache write and prefill attention"}
+    except Exception as e:  # reported in the line, same on every rank
+        out["prefill_8192_int4"] = {"error": repr(e)[:300]}
+    del dec
+    torch.cuda.empty_cache()
+    if world == 1:
+        out["decode_b64_int4_64k"] = {"skipped": "64 layers x 64 sequences x 64k tokens of int4 KV need 285 GB: "
+                                                 "measured from 2 GPUs on"}
+        return out
+    try:
+        dec = SyntheticDecoder(shape, dev, batch=64, q_len=1, ctx=65536, seed=2024, tp_size=world, tp_rank=rank,
+                               group=pg, kv_cache="int4")
+        tokens = torch.randint(0, shape.vocab, (64,), device=dev)
+        ms = timed(lambda: dec.step(tokens))
+        wb, kb = dec.weight_bytes(), dec.kv_bytes()
+        out["decode_b64_int4_64k"] = {"batch": 64, "ctx": 65536, "ms_per_step": ms, "tok_s": 64 / (ms * 1e-3),
+                                      "tp": world, "weight_bytes": wb, "kv_bytes": kb,
+                                      "gb_s": (wb + kb) / (ms * 1e-3) / 1e9,
+                                      "note": "eager; linears through exl3b_gemm (64 rows), int4 split-KV attention"}
+        del dec
+    except Exception as e:
+        out["decode_b64_int4_64k"] = {"error": repr(e)[:300]}
+    torch.cuda.empty_cache()
+    return out
+
+
+def parity_check(torch, dev, world: int, rank: int, pg, comm) -> dict:
+    """Untimed correctness of what the line measures.  One GPU: a small linear and an int8 attention
+    against the CPU oracle.  N GPUs: one decoder layer's linears with weights drawn whole and sharded
+    (column-parallel outputs gathered, row-parallel ones reduced inside the GEMV) against the
+    single-GPU op on the whole weights, and a 2-layer synthetic decode step's logits at TP N against
+    the same model on one GPU; gate nRMS <= 1e-3, cosine >= 0.99999."""
+    def cmp(got, ref):
+        got, ref = got.double().flatten(), ref.double().flatten()
+        e = float((got - ref).pow(2).mean().sqrt() / ref.pow(2).mean().sqrt())
+        c = float(torch.nn.functional.cosine_similarity(got, ref, 0))
+        return {"nrms": e, "cos": c, "ok": bool(e <= 1e-3 and c >= 0.99999)}
+
+    res = {}
+    if world == 1:
+        from oracle import exl3_oracle as O
+        rng = np.random.default_rng(3)
+        k, n, K = 1024, 512, 4
+        tr = O.random_trellis(rng, k // 16, n // 16, K)
+        suh = np.sign(rng.standard_normal(k)).astype(np.float16)
+        svh = np.sign(rng.standard_normal(n)).astype(np.float16)
+        for m in (1, 64):
+            x = (rng.standard_normal((m, k)) * 0.3).astype(np.float16)
+            y = torch.ops.exl3rocm.linear(torch.from_numpy(x).to(dev), torch.from_numpy(tr.view(np.int16)).to(dev),
+                                          torch.from_numpy(suh).to(dev), torch.from_numpy(svh).to(dev), K, False, True)
+            res[f"linear_m{m}_vs_oracle"] = cmp(y.cpu(), torch.from_numpy(O.linear(x, tr, K, suh, svh, 2)))
+    else:
+        from exl3rocm.synthetic import DecoderShape, Layer, SyntheticDecoder
+        from exl3rocm.tp import linear_tp
+        shape = DecoderShape()
+        g1, g2 = torch.Generator(device=dev), torch.Generator(device=dev)
+        g1.manual_seed(77)
+        g2.manual_seed(77)
+        full = Layer(g1, shape, dev)
+        part = Layer(g2, shape, dev, tp=world, rank=rank)
+        gx = torch.Generator(device=dev)
+        gx.manual_seed(78)
+        x = torch.randn((4, shape.hidden), generator=gx, device=dev).half()
+        xi = torch.randn((4, shape.intermediate), generator=gx, device=dev).half()
+        for name in ("q", "gate"):  # column-parallel: gather the ranks' columns
+            w, wp = getattr(full, name), getattr(part, name)
+            ref = torch.ops.exl3rocm.linear(x, w.trellis, w.suh, w.svh, w.K, False, True)
+            mine = torch.ops.exl3rocm.linear(x, wp.trellis, wp.suh, wp.svh, wp.K, False, True).contiguous()
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            torch.distributed.all_gather(parts, mine, group=pg)
+            res[f"{name}_column_parallel"] = cmp(torch.cat(parts, 1), ref)
+        for name, xin in (("o", x), ("down", xi)):  # row-parallel: the in-kernel reduction
+            w, wp = getattr(full, name), getattr(part, name)
+            ref = torch.ops.exl3rocm.linear(xin, w.trellis, w.suh, w.svh, w.K, False, True)
+            kl = xin.shape[1] // world
+            mine = linear_tp(xin[:, rank * kl:(rank + 1) * kl], wp.trellis, wp.suh, wp.svh, wp.K, False, True, comm)
+            res[f"{name}_row_parallel"] = cmp(mine, ref)
+        del full, part
+        small = DecoderShape(layers=2)
+        one = SyntheticDecoder(small, dev, batch=2, q_len=1, ctx=1024, seed=5)
+        tpd = SyntheticDecoder(small, dev, batch=2, q_len=1, ctx=1024, seed=5, tp_size=world, tp_rank=rank,
+                               comm=comm, group=pg)
+        tokens = torch.arange(2, device=dev) * 7919
+        one.step(tokens)
+        tpd.step(tokens)
+        lg = tpd.logits.contiguous()
+        sizes = [None] * world
+        torch.distributed.all_gather_object(sizes, lg.shape[1], group=pg)
+        parts = [torch.empty((lg.shape[0], w), dtype=lg.dtype, device=dev) for w in sizes]
+        torch.distributed.all_gather(parts, lg, group=pg)
+        res["decode_step_logits"] = cmp(torch.cat(parts, 1), one.logits)
+        del one, tpd
+        torch.cuda.empty_cache()
+    res["ok"] = all(v["ok"] for v in res.values())
+    return res
+
+
 # ---------------------------------------------------------------------------------------------
 # main
 # ---------------------------------------------------------------------------------------------
@@ -676,9 +814,14 @@ def main():
 
     extra = {}
     if world == 1 and not args.no_extra:
-        extra["kv_attention"] = [bench_kv(torch, dev, kind, ctx, b, ql)
-                                 for kind, ctx, b, ql in ((8, 32768, 8, 1), (4, 32768, 8, 1), (8, 32768, 1, 4),
-                                                          (4, 65536, 1, 1), (8, 4096, 8, 1), (8, 32768, 1, 1))]
+        cases = [(kind, ctx, b, 1) for kind in (8, 4) for ctx in (4096, 32768, 65536) for b in (1, 8)]
+        cases += [(8, 32768, 1, 4), (4, 32768, 1, 4)]  # speculative verify, 4 query tokens
+        extra["kv_attention"] = []
+        for kind, ctx, b, ql in cases:
+            rec = bench_kv(torch, dev, kind, ctx, b, ql)
+            rec["roofline"] = {"bound": "hbm", "frac": rec["gb_s"] / hbm_peak, "peak": hbm_peak, "unit": "GB/s"}
+            extra["kv_attention"].append(rec)
+            torch.cuda.empty_cache()
         extra["prefill_m2048"] = bench_prefill(torch, dev, K, peak_tflops=float(peaks.get("bf16_tflops", 1590.0)))
         extra["sweep"] = bench_sweep(torch, dev)
 
@@ -692,6 +835,18 @@ def main():
             extra["decode"] = {"error": repr(e)[:300]}
             torch.cuda.synchronize()
             torch.cuda.empty_cache()
+
+    if not args.no_extra:
+        try:
+            extra["c5"] = bench_c5(torch, dev, world, rank, pg, comm)
+        except Exception as e:
+            extra["c5"] = {"error": repr(e)[:300]}
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+    try:
+        extra["parity"] = parity_check(torch, dev, world, rank, pg, comm)
+    except Exception as e:
+        extra["parity"] = {"ok": False, "error": repr(e)[:300]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

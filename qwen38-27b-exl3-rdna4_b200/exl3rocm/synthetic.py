@@ -19,6 +19,13 @@ seven of this library's launches per layer.  fused=False runs the same step with
 RoPE and KV-write launches (ten per layer), for comparison.  All buffers are allocated up front, so
 the step can be captured in a CUDA graph.
 
+The KV cache is int8 (default) or int4 per-token-head (kv="int4": nibble rows, zero point in the
+scale word, RHT domain, the exact rows off).  A step of more than 16 rows (batched decode, e.g. 64
+sequences) runs its linears through the tcgen05 GEMM (exl3b_gemm) with separate RMSNorm, SiLU * up and
+residual adds, since the fused epilogues are those of the 1..16-row GEMV.  ``prefill`` runs one
+prompt eagerly through the same layers: GEMM linears, RoPE, the cache write of every prompt token and
+the prefill attention over the quantised cache (gather + fp16 attention).
+
 Tensor parallel (tp_size > 1, one process per GPU): every rank draws the whole model from the same
 seed, layer by layer, and keeps its shard, so the sharded model is the single-GPU model.  q/k/v
 are split by heads and gate/up by columns (no exchange); o and down by their inputs, summed across
@@ -136,22 +143,29 @@ class SyntheticDecoder:
 
     def __init__(self, shape: DecoderShape, device, batch: int = 1, q_len: int = 1, ctx: int = 32768,
                  seed: int = 0, weights_of: "SyntheticDecoder | None" = None, tp_size: int = 1, tp_rank: int = 0,
-                 comm=None, group=None, fused: bool = True):
+                 comm=None, group=None, fused: bool = True, kv_cache: str = "int8",
+                 gemm_linears: bool | None = None):
         """weights_of: take the weights of another decoder of the same shape and sharding (a different
-        batch, query length or context over the same model)."""
+        batch, query length or context over the same model).  kv_cache: "int8" or "int4".
+        gemm_linears: run the step's linears through the GEMM route (default: when M > 16)."""
         s = self.s = shape
         self.device = device = torch.device(device)
         self.batch, self.q_len, self.ctx = batch, q_len, ctx
         self.tp, self.rank, self.comm, self.group = tp_size, tp_rank, comm, group
         self.fused = fused
         M = self.M = batch * q_len
-        if M > ops.GEMV_MAX_ROWS:
-            raise ValueError(f"decode step of {M} rows: the fused linears take 1..{ops.GEMV_MAX_ROWS}")
+        if kv_cache not in ("int8", "int4"):
+            raise ValueError(f"kv_cache {kv_cache!r}: int8 or int4")
+        self.kv_kind = kv_cache
+        # GEMM linears, separate norm / activation / residual adds
+        self.batched = M > ops.GEMV_MAX_ROWS if gemm_linears is None else bool(gemm_linears)
+        if self.batched and q_len != 1:
+            raise ValueError("batched steps are decode steps (q_len 1)")
         if ctx % s.block_size or q_len > ctx:
             raise ValueError("ctx must be a multiple of the block size and >= q_len")
         tp = tp_size
         if tp > 1:
-            if comm is None:
+            if comm is None and not self.batched:
                 raise ValueError("tensor parallel decode needs a TpComm")
             if s.q_heads % tp or s.kv_heads % tp or (s.intermediate // 128) % tp:
                 raise ValueError(f"heads and intermediate blocks must divide by tp {tp}")
@@ -178,14 +192,23 @@ class SyntheticDecoder:
         nblk = batch * bps
         h0, h1 = tp_rank * self.hkv, (tp_rank + 1) * self.hkv
         self.k_cache, self.v_cache, self.k_scale, self.v_scale = [], [], [], []
+        row = s.head if kv_cache == "int8" else s.head // 2
         for _ in range(s.layers):
             for dst, is_rows in ((self.k_cache, True), (self.v_cache, True), (self.k_scale, False),
                                  (self.v_scale, False)):
-                if is_rows:
-                    full = torch.randint(-127, 128, (nblk, s.block_size, s.kv_heads, s.head), generator=gen,
+                if is_rows and kv_cache == "int8":
+                    full = torch.randint(-127, 128, (nblk, s.block_size, s.kv_heads, row), generator=gen,
                                          device=device, dtype=torch.int8)
-                else:
+                elif is_rows:  # packed nibbles
+                    full = torch.randint(0, 256, (nblk, s.block_size, s.kv_heads, row), generator=gen,
+                                         device=device, dtype=torch.int32).to(torch.uint8)
+                elif kv_cache == "int8":
                     full = torch.rand((nblk, s.block_size, s.kv_heads), generator=gen, device=device) * 0.02
+                else:  # scale word: (fp32 scale & ~0xF) | zero point
+                    sc = torch.rand((nblk, s.block_size, s.kv_heads), generator=gen, device=device) * 0.3 + 0.05
+                    zp = torch.randint(4, 12, sc.shape, generator=gen, device=device, dtype=torch.int32)
+                    full = ((sc.view(torch.int32) & ~0xF) | zp).view(torch.float32)
+                    del sc, zp
                 dst.append(full if tp == 1 else full[:, :, h0:h1].contiguous())
                 del full
         self.block_table = torch.arange(nblk, dtype=torch.int32, device=device).view(batch, bps)
@@ -205,6 +228,9 @@ class SyntheticDecoder:
         self.q = torch.empty(M, qd, dtype=torch.float16, device=device)
         self.attn = torch.empty(M, qd, dtype=torch.float16, device=device)
         self.act = torch.empty(M, s.intermediate // tp, dtype=torch.float16, device=device)
+        if self.batched or kv_cache == "int4":
+            self.gu = torch.empty(M, 2 * s.intermediate // tp, dtype=torch.float16, device=device)
+            self.row_out = torch.empty(M, s.hidden, dtype=torch.float16, device=device)
         self.logits = torch.empty(M, self.v1 - self.v0, dtype=torch.float16, device=device)
         self.next_tokens = torch.empty(M, dtype=torch.int64, device=device)
         if tp > 1:
@@ -221,7 +247,10 @@ class SyntheticDecoder:
         with ctx:
             for k, n, g in ((s.hidden, qd + 2 * kd, 3), (qd, s.hidden, 1), (s.hidden, 2 * it, 2),
                             (it, s.hidden, 1), (s.hidden, self.v1 - self.v0, 1)):
-                ops.reserve_workspace(dev, k, n, g, M)
+                if self.batched:
+                    ops.reserve_gemm_workspace(dev, M, k)
+                else:
+                    ops.reserve_workspace(dev, k, n, g, M)
             kv.reserve_attention_workspace(dev, M, self.hq, self.batch, self.hkv, self.ctx)
 
     def weight_bytes(self) -> int:
@@ -229,13 +258,83 @@ class SyntheticDecoder:
         return self.s.layers * self.s.layer_bytes() + self.s.hidden * self.s.vocab * self.s.bits_head // 8
 
     def kv_bytes(self) -> int:
-        """KV cache bytes the attention reads per step, all ranks together (int8 rows + fp32 scales)."""
+        """KV cache bytes the attention reads per step, all ranks together (K and V rows + fp32 scales)."""
         s = self.s
-        return s.layers * self.batch * self.ctx * s.kv_heads * (2 * s.head + 8)
+        row = s.head if self.kv_kind == "int8" else s.head // 2
+        return s.layers * self.batch * self.ctx * s.kv_heads * (2 * row + 8)
+
+    def _attention(self, i: int, q: torch.Tensor, out: torch.Tensor, seq_lens, cu_q, max_q: int, max_k: int,
+                   block_table=None) -> None:
+        s = self.s
+        fn = kv.attention_int8 if self.kv_kind == "int8" else kv.attention
+        fn(q=q, k=self.k_cache[i], v=self.v_cache[i], out=out, cu_seqlens_q=cu_q, max_seqlen_q=max_q,
+           seqused_k=seq_lens, block_table=self.block_table if block_table is None else block_table,
+           softmax_scale=1.0 / math.sqrt(s.head), k_scale_cache=self.k_scale[i], v_scale_cache=self.v_scale[i],
+           max_seqlen_k=max_k)
+
+    def _write_cache(self, i: int, qkv: torch.Tensor, slots: torch.Tensor) -> None:
+        s = self.s
+        qd, kd = self.hq * s.head, self.hkv * s.head
+        T = qkv.shape[0]
+        key = qkv[:, qd:qd + kd].view(T, self.hkv, s.head)
+        val = qkv[:, qd + kd:].view(T, self.hkv, s.head)
+        if self.kv_kind == "int8":
+            kv.reshape_and_cache_int8(key, val, self.k_cache[i], self.v_cache[i], slots, self.k_scale[i],
+                                      self.v_scale[i])
+        else:
+            kv.reshape_and_cache(key, val, self.k_cache[i], self.v_cache[i], slots, k_scale_cache=self.k_scale[i],
+                                 v_scale_cache=self.v_scale[i])
+
+    def _large_layer(self, i: int, x_res: torch.Tensor, qkv: torch.Tensor, q: torch.Tensor, attn: torch.Tensor,
+                     positions: torch.Tensor, slots: torch.Tensor, attend) -> None:
+        """One layer for many rows: RMSNorm, GEMM linears (exl3b_gemm), RoPE, the cache write, attention
+        (``attend``), residual adds; under tensor parallelism the row-parallel partial outputs are summed
+        with an NCCL all-reduce."""
+        s, L = self.s, self.layers[i]
+        h = rmsnorm(x_res, L.norm_in, s.eps)
+        self._gemm_into(h, [L.q, L.k, L.v], s.bits_qkv, qkv)
+        rope_neox(qkv, q, self.hq, self.hkv, positions, self.cos_sin)
+        self._write_cache(i, qkv, slots)
+        attend(i, q.view(-1, self.hq, s.head), attn.view(-1, self.hq, s.head))
+        self._row_add(x_res, attn, L.o, s.bits_o)
+        h = rmsnorm(x_res, L.norm_post, s.eps)
+        gu = torch.empty(h.shape[0], 2 * L.gate.n, dtype=torch.float16, device=h.device)
+        self._gemm_into(h, [L.gate, L.up], s.bits_gate_up, gu)
+        act = ops.silu_mul(gu)
+        self._row_add(x_res, act, L.down, s.bits_down)
+
+    @staticmethod
+    def _gemm_into(x: torch.Tensor, ws: list, K: int, out: torch.Tensor) -> None:
+        """The GEMM route (exl3b_gemm) of each weight into its column slice of out."""
+        n0 = 0
+        for w in ws:
+            ops._linear_large(x, w.trellis, w.suh, w.svh, K, *CB, out[:, n0:n0 + w.n])
+            n0 += w.n
+
+    def _row_add(self, x_res: torch.Tensor, x: torch.Tensor, w: Exl3Weight, K: int) -> None:
+        y = torch.empty(x.shape[0], w.n, dtype=torch.float16, device=x.device)
+        self._gemm_into(x, [w], K, y)
+        if self.tp > 1:
+            torch.distributed.all_reduce(y, group=self.group)
+        x_res.add_(y)
 
     def layer_forward(self, i: int) -> None:
         s, L = self.s, self.layers[i]
         qd, kd, M = self.hq * s.head, self.hkv * s.head, self.M
+        if self.batched:
+            self._large_layer(i, self.residual, self.qkv, self.q, self.attn, self.positions, self.slot_mapping,
+                              lambda j, qq, out: self._attention(j, qq, out, self.seq_lens, self.cu_q, 1, self.ctx))
+            return
+        if self.kv_kind == "int4":
+            self._normed_linear(L.norm_in, [L.q, L.k, L.v], s.bits_qkv, self.qkv)
+            rope_neox(self.qkv, self.q, self.hq, self.hkv, self.positions, self.cos_sin)
+            self._write_cache(i, self.qkv, self.slot_mapping)
+            self._attention(i, self.q.view(M, self.hq, s.head), self.attn.view(M, self.hq, s.head), self.seq_lens,
+                            self.cu_q, self.q_len, self.ctx)
+            self._row_parallel(self.attn, L.o, s.bits_o)
+            self._normed_linear(L.norm_post, [L.gate, L.up], s.bits_gate_up, self.act, ops.ACT_SILU_MUL)
+            self._row_parallel(self.act, L.down, s.bits_down)
+            return
         mcg, mul1 = CB
         self._normed_linear(L.norm_in, [L.q, L.k, L.v], s.bits_qkv, self.qkv)
         if self.fused:
@@ -282,7 +381,12 @@ class SyntheticDecoder:
         torch.index_select(self.embed, 0, tokens, out=self.residual)
         for i in range(s.layers):
             self.layer_forward(i)
-        self._normed_linear(self.norm_final, [self.head], s.bits_head, self.logits)
+        if self.batched:
+            self.logits.copy_(torch.ops.exl3rocm.linear(rmsnorm(self.residual, self.norm_final, s.eps),
+                                                        self.head.trellis, self.head.suh, self.head.svh, s.bits_head,
+                                                        *CB))
+        else:
+            self._normed_linear(self.norm_final, [self.head], s.bits_head, self.logits)
         if self.tp == 1:
             torch.argmax(self.logits, dim=-1, out=self.next_tokens)
         else:
@@ -297,10 +401,55 @@ class SyntheticDecoder:
             self.next_tokens.copy_(p[:, :, 1].gather(0, best[None, :])[0].long())
         return self.next_tokens
 
+    def prefill(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Prefill of one prompt (tokens int64 [P], P <= ctx) into sequence 0's cache, eagerly: per layer
+        RMSNorm, the GEMM linears, RoPE, the cache write of all P tokens, causal prefill attention over
+        the quantised cache (kv.prefill_int8 / kv.prefill: the blocks dequantised to fp16 once, then
+        fp16 attention), SiLU * up and the residual adds; then the last token's logits.  Returns the
+        greedy next token."""
+        s, P = self.s, tokens.shape[0]
+        if P > self.ctx:
+            raise ValueError(f"prompt of {P} tokens for a cache of {self.ctx}")
+        dev = self.device
+        qd, kd = self.hq * s.head, self.hkv * s.head
+        res = torch.index_select(self.embed, 0, tokens)
+        qkv = torch.empty(P, qd + 2 * kd, dtype=torch.float16, device=dev)
+        q = torch.empty(P, qd, dtype=torch.float16, device=dev)
+        attn = torch.empty(P, qd, dtype=torch.float16, device=dev)
+        pos = torch.arange(P, dtype=torch.int64, device=dev)
+        slots = self.block_table[0].to(torch.int64)[pos // s.block_size] * s.block_size + pos % s.block_size
+        seq = torch.tensor([P], dtype=torch.int32, device=dev)
+        cu = torch.tensor([0, P], dtype=torch.int32, device=dev)
+        bt = self.block_table[:1]
+
+        def attend(i, qq, out):
+            kw = dict(q=qq, k=self.k_cache[i], v=self.v_cache[i], out=out, cu_seqlens_q=cu, max_seqlen_q=P,
+                      seqused_k=seq, max_seqlen_k=P, block_table=bt, softmax_scale=1.0 / math.sqrt(s.head),
+                      k_scale_cache=self.k_scale[i], v_scale_cache=self.v_scale[i])
+            if self.kv_kind == "int8":
+                kv.prefill_int8(None, kw)
+            else:
+                kv.prefill(None, kw)
+
+        for i in range(s.layers):
+            self._large_layer(i, res, qkv, q, attn, pos, slots, attend)
+        last = rmsnorm(res[-1:], self.norm_final, s.eps)
+        logits = torch.ops.exl3rocm.linear(last, self.head.trellis, self.head.suh, self.head.svh, s.bits_head, *CB)
+        self.prefill_logits = logits
+        return torch.argmax(logits, dim=-1)
+
     def launches_per_step(self) -> int:
-        """This library's kernel launches in one step: per layer 4 linears (norms fused), rope + KV write,
-        the attention and its split combine, then the lm_head; unfused: 3 more per layer, 1 more at the end."""
-        return self.s.layers * 7 + 1 if self.fused else self.s.layers * 10 + 2
+        """This library's kernel launches in one step.  int8, 1..16 rows: per layer 4 linears (norms
+        fused), rope + KV write, the attention and its split combine, then the lm_head; unfused: 3 more
+        per layer, 1 more at the end.  int4 adds a separate RoPE and the q rotation (9 per layer).
+        Batched (GEMM) steps: 2 RMSNorms, 7 GEMMs with their had_in, RoPE, write, attention (+ combine,
+        + q rotation for int4), SiLU * up per layer; final norm and lm_head."""
+        L = self.s.layers
+        if self.batched:
+            return L * (2 + 2 * 7 + 1 + 1 + (2 if self.kv_kind == "int8" else 3) + 1) + 3
+        if self.kv_kind == "int4":
+            return L * 9 + 1
+        return L * 7 + 1 if self.fused else L * 10 + 2
 
 
 def main(argv=None) -> None:
