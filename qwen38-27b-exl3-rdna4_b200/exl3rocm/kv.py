@@ -377,11 +377,17 @@ def _sdpa_paged(q, kd, vd, cu_seqlens_q, seqused_k, nb, softmax_scale, out):
         ql = q1 - q0
         k = kd[s * nb:(s + 1) * nb].reshape(nb * bs, kd.shape[2], HEAD_SIZE)[:L]
         v = vd[s * nb:(s + 1) * nb].reshape(nb * bs, vd.shape[2], HEAD_SIZE)[:L]
-        # query i sits at position L - ql + i and sees keys 0 .. L - ql + i
-        mask = torch.arange(L, device=q.device)[None, :] <= (L - ql + torch.arange(ql, device=q.device))[:, None]
+        # query i sits at position L - ql + i and sees keys 0 .. L - ql + i: for a whole prompt (ql == L)
+        # that is the plain causal mask, which keeps SDPA on its fused kernels; a chunk after cached
+        # context needs the shifted mask
+        if ql == L:
+            mask, causal = None, True
+        else:
+            mask = torch.arange(L, device=q.device)[None, :] <= (L - ql + torch.arange(ql, device=q.device))[:, None]
+            causal = False
         o = torch.nn.functional.scaled_dot_product_attention(
-            q[q0:q1].transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), attn_mask=mask, scale=softmax_scale,
-            enable_gqa=True)
+            q[q0:q1].transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), attn_mask=mask, is_causal=causal,
+            scale=softmax_scale, enable_gqa=True)
         out[q0:q1] = o.transpose(0, 1).to(out.dtype)
 
 

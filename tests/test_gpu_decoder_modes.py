@@ -72,7 +72,7 @@ def test_batched_step_of_32_rows(syn):
 @pytest.mark.parametrize("kv_cache", ["int8", "int4"])
 def test_prefill_then_decode(syn, kv_cache):
     shape = syn.DecoderShape(**SMALL)
-    P = 200
+    P = 208  # a multiple of the block size
     dec = syn.SyntheticDecoder(shape, DEV, batch=1, q_len=1, ctx=P, seed=23, kv_cache=kv_cache)
     prompt = torch.randint(0, shape.vocab, (P,), device=DEV)
     nxt = dec.prefill(prompt)
