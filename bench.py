@@ -551,12 +551,14 @@ def parity_check(torch, dev, world: int, rank: int, pg, comm) -> dict:
     against the CPU oracle.  N GPUs: one decoder layer's linears with weights drawn whole and sharded
     (column-parallel outputs gathered, row-parallel ones reduced inside the GEMV) against the
     single-GPU op on the whole weights, and a 2-layer synthetic decode step's logits at TP N against
-    the same model on one GPU; gate nRMS <= 1e-3, cosine >= 0.99999."""
-    def cmp(got, ref):
+    the same model on one GPU.  Gates: nRMS <= 1e-3 and cosine >= 0.99999 for a linear; for the logits,
+    which pass two layers of fp16 activations whose o / down sums differ in fp32 order and in where the
+    residual add rounds (inside the TP epilogue, against after the single-GPU op), nRMS <= 2e-3."""
+    def cmp(got, ref, tol=1e-3):
         got, ref = got.double().flatten(), ref.double().flatten()
         e = float((got - ref).pow(2).mean().sqrt() / ref.pow(2).mean().sqrt())
         c = float(torch.nn.functional.cosine_similarity(got, ref, 0))
-        return {"nrms": e, "cos": c, "ok": bool(e <= 1e-3 and c >= 0.99999)}
+        return {"nrms": e, "cos": c, "tol": tol, "ok": bool(e <= tol and c >= 0.99999)}
 
     res = {}
     if world == 1:
@@ -610,7 +612,7 @@ def parity_check(torch, dev, world: int, rank: int, pg, comm) -> dict:
         torch.distributed.all_gather_object(sizes, lg.shape[1], group=pg)
         parts = [torch.empty((lg.shape[0], w), dtype=lg.dtype, device=dev) for w in sizes]
         torch.distributed.all_gather(parts, lg, group=pg)
-        res["decode_step_logits"] = cmp(torch.cat(parts, 1), one.logits)
+        res["decode_step_logits"] = cmp(torch.cat(parts, 1), one.logits, 2e-3)
         del one, tpd
         torch.cuda.empty_cache()
     res["ok"] = all(v["ok"] for v in res.values())
