@@ -316,6 +316,71 @@ def bench_kv(torch, dev, kind: int, ctx: int, batch: int, q_len: int, iters: int
             "gb_s": kv_bytes / (ms * 1e-3) / 1e9, "kv_bytes": kv_bytes}
 
 
+def bench_kv_write(torch, dev, kind: int, tokens: int, iters: int = 20) -> dict:
+    """One cache write of `tokens` K and V rows (8 kv heads x 128, fp16, N(0,1) with 1 % of channels x8)
+    into an int8 or int4 paged cache, slots in a random block order.  GB/s counts the fp16 rows read
+    and the codes and scales written."""
+    from exl3rocm import kv as xkv
+    nblk = (tokens + KV_BS - 1) // KV_BS
+    row_bytes = KV_D if kind == 8 else KV_D // 2
+    kc = torch.zeros((nblk, KV_BS, KV_HKV, row_bytes), dtype=torch.int8 if kind == 8 else torch.uint8, device=dev)
+    vc = torch.zeros_like(kc)
+    ks = torch.zeros((nblk, KV_BS, KV_HKV), dtype=torch.float32, device=dev)
+    vs = torch.zeros_like(ks)
+    g = torch.Generator(device=dev)
+    g.manual_seed(57 + tokens)
+    k = torch.randn((tokens, KV_HKV, KV_D), generator=g, device=dev)
+    v = torch.randn((tokens, KV_HKV, KV_D), generator=g, device=dev)
+    ch = torch.randperm(KV_D, generator=g, device=dev)[: max(1, KV_D // 100)]
+    k[..., ch] *= 8
+    v[..., ch] *= 8
+    k, v = k.half(), v.half()
+    blk = torch.randperm(nblk, generator=g, device=dev)
+    pos = torch.arange(tokens, device=dev)
+    slots = blk[pos // KV_BS] * KV_BS + pos % KV_BS
+    if kind == 8:
+        call = lambda: xkv.reshape_and_cache_int8(k, v, kc, vc, slots, ks, vs)
+    else:
+        xkv.configure_request_slots(1)
+        xkv._req["slot"] = None
+        xkv._exact.pop("bench_write", None)
+        xkv.set_batch_slots(torch.zeros(1, dtype=torch.int32, device=dev))
+        qsl = torch.tensor([0, tokens], dtype=torch.int32, device=dev)
+        sl = torch.tensor([tokens], dtype=torch.int32, device=dev)
+        call = lambda: xkv.reshape_and_cache(k, v, kc, vc, slots, k_scale_cache=ks, v_scale_cache=vs,
+                                             layer_name="bench_write", query_start_loc=qsl, seq_lens=sl)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    call()
+    ms = _event_ms(torch, call, iters, flush)
+    nbytes = tokens * KV_HKV * (2 * 2 * KV_D + 2 * row_bytes + 8)
+    del kc, vc, ks, vs, flush
+    return {"cache": f"int{kind}", "tokens": tokens, "ms": ms, "gb_s": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes}
+
+
+def bench_decode_ceiling(torch, dev, K: int, iters: int = 4000, reps: int = 5) -> dict:
+    """exl3b_decode_ceiling: the GEMV's per-tile decode + mma with the trellis resident in shared
+    memory (no HBM, no stage hand-offs), one CTA of 16 warps per SM.  Its tile rate, in the GB/s of
+    trellis it would consume at K bits, bounds what this decode can stream from HBM."""
+    import ctypes
+    from exl3rocm import _lib
+    L = _lib.lib()
+    g = torch.Generator(device=dev)
+    g.manual_seed(41 + K)
+    tr = torch.randint(-32768, 32768, (8 * 64 * 16 * K,), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    out = torch.empty(sms * 512, dtype=torch.float32, device=dev)
+    ctas = ctypes.c_int(0)
+    st = torch.cuda.current_stream().cuda_stream
+    call = lambda: L.exl3b_decode_ceiling(K, 2, tr.data_ptr(), iters, out.data_ptr(), ctypes.byref(ctas), st)
+    for _ in range(3):
+        rc = call()
+        assert rc == 0, rc
+    ms = _event_ms(torch, call, reps)
+    tiles = ctas.value * 16 * iters * 32
+    return {"bits": K, "ctas": ctas.value, "ms": ms, "tiles_per_s": tiles / (ms * 1e-3),
+            "gb_s": tiles * 32 * K / (ms * 1e-3) / 1e9, "finite": bool(torch.isfinite(out).all().item())}
+
+
 def _layer_weights(torch, dev, k, n, K, seed):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
@@ -638,8 +703,28 @@ def main():
                          "or an NCCL all-reduce after it")
     ap.add_argument("--modules", default="qkv,o,gate_up,down",
                     help="comma list of the layer's modules a step runs (default: all four)")
+    ap.add_argument("--only", default=None,
+                    help="run one leg alone and print its record (for profiler captures): "
+                         "kv:<8|4>:<ctx>:<batch>:<q_len>, kv_write:<8|4>:<tokens>, ceiling:<K>")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
+    if args.only:
+        import torch
+        sys.path.insert(0, os.path.join(ROOT, "qwen38-27b-exl3-rdna4_b200"))
+        import exl3rocm.ops  # noqa: F401
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        kind, *a = args.only.split(":")
+        if kind == "kv":
+            rec = bench_kv(torch, dev, *map(int, a), iters=args.steps)
+        elif kind == "kv_write":
+            rec = bench_kv_write(torch, dev, *map(int, a), iters=args.steps)
+        elif kind == "ceiling":
+            rec = bench_decode_ceiling(torch, dev, int(a[0]), reps=args.steps)
+        else:
+            raise SystemExit(f"unknown leg {kind}")
+        print(json.dumps({"only": args.only, **rec}))
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -824,6 +909,18 @@ def main():
             rec["roofline"] = {"bound": "hbm", "frac": rec["gb_s"] / hbm_peak, "peak": hbm_peak, "unit": "GB/s"}
             extra["kv_attention"].append(rec)
             torch.cuda.empty_cache()
+        extra["kv_write"] = []
+        for kind in (8, 4):
+            rec = bench_kv_write(torch, dev, kind, 8192)
+            rec["roofline"] = {"bound": "hbm", "frac": rec["gb_s"] / hbm_peak, "peak": hbm_peak, "unit": "GB/s"}
+            extra["kv_write"].append(rec)
+        extra["decode_ceiling"] = []
+        for kb in (2, 3, 4, 5, 6, 8):
+            rec = bench_decode_ceiling(torch, dev, kb)
+            rec["frac_of_hbm"] = rec["gb_s"] / hbm_peak
+            if kb == K:
+                rec["gemv_gate_up_frac_of_ceiling"] = achieved / rec["gb_s"]
+            extra["decode_ceiling"].append(rec)
         extra["prefill_m2048"] = bench_prefill(torch, dev, K, peak_tflops=float(peaks.get("bf16_tflops", 1590.0)))
         extra["sweep"] = bench_sweep(torch, dev)
 

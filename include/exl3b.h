@@ -117,6 +117,16 @@ EXL3B_API int exl3b_linear_grouped(const uint16_t* x, int m, int k, int groups, 
                          const uint16_t* const* svh, uint16_t* const* y, int64_t ldy,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode-ceiling microbenchmark of the decode GEMV (no reference counterpart): one CTA per SM runs
+ * the GEMV's per-tile work (trellis words from shared memory, window extraction, codebook decode into
+ * mma A fragments, one m16n8k16 per 16x16 tile) over one resident stage of 8 k-rows x 64 tiles,
+ * `iters` times, with no HBM traffic and no stage hand-offs.  Each launch decodes
+ * (*ctas) x 16 warps x iters x 32 tiles; time it with events on `stream`.  trellis: at least
+ * 8 x 64 x 32K bytes (16-byte aligned); out: (*ctas) x 512 floats (the accumulators' sums, which
+ * keep the work live); *ctas receives the SM count used. */
+EXL3B_API int exl3b_decode_ceiling(int K, int codebook, const uint16_t* trellis, int iters, float* out, int* ctas,
+                                   void* stream);
+
 /* Workspace of exl3b_gemm: a 256-byte header (error word at offset 0) plus A_had [m][k] fp16. */
 EXL3B_API size_t exl3b_gemm_workspace_bytes(int m, int k);
 

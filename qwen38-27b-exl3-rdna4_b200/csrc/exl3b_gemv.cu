@@ -42,9 +42,13 @@ constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summ
 constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
 constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
 
-// trellis k-tile slots per unit (64 tiles each): 32-64 KB of trellis per stage.  Larger units
-// measured faster than 32 KB ones despite coarser stream-K granularity (fewer unit hand-offs).
-__host__ __device__ constexpr int rows_per_unit(int K) { return K <= 4 ? 8 : 2; }
+// trellis k-tile slots per unit (64 tiles each) at K <= 4; K > 4 takes 2.
+#ifndef EXL3B_GEMV_R0_SMALLK
+#define EXL3B_GEMV_R0_SMALLK 8
+#endif
+constexpr int kR0SmallK = EXL3B_GEMV_R0_SMALLK;
+static_assert(kR0SmallK == 2 || kR0SmallK == 4 || kR0SmallK == 8, "rows per unit");
+__host__ __device__ constexpr int rows_per_unit(int K) { return K <= 4 ? kR0SmallK : 2; }
 constexpr int kMaxUnitRows = 16;  // k-rows of one unit at most (R0 * q), bounding the A_had area
 
 struct GemvGroups {
@@ -132,9 +136,10 @@ EXL3B_DEV SbInfo sb_info(const GemvGroups& gg, int groups, int sb) {
 // ---------------------------------------------------------------------------------------------
 // launch 2: the stream-K decode GEMV
 // ---------------------------------------------------------------------------------------------
-// Shared memory: a ring of kStages stages (R trellis rows of up to 64 tiles at a fixed stride,
-// then the unit's A_had rows), the fp32 accumulator tile [8 MT rows][kAccCols] where the decode
-// warps pool a finished super-block, and the mbarriers.
+// Shared memory: a ring of `stages` stages (R trellis rows of up to 64 tiles at a fixed stride,
+// then the unit's A_had rows), the fp32 accumulator tile [m rows][kAccCols] where the decode
+// warps pool a finished super-block, and the mbarriers.  The stage size is fixed by K, MT and R0;
+// the tile has one row per input row, so that few rows leave room for a deeper ring.
 template <int K, int MT, int R0_>
 struct GemvSmem {
     static constexpr int R0 = R0_;                         // stage slots of 64 tiles
@@ -143,19 +148,32 @@ struct GemvSmem {
     static constexpr int kTrellisStage = R0 * kRowBytes;
     static constexpr int kAhadStage = (R0 * 4 > kMaxUnitRows ? kMaxUnitRows : R0 * 4) * 8 * MT * 32;  // k-tiles x 8 MT rows x 16 halves
     static constexpr int kStageBytes = kTrellisStage + kAhadStage;
-    static constexpr int kAccBytes = 8 * MT * kAccCols * 4;
     static constexpr int kBudget = 220 * 1024;
-    static constexpr int kStages0 = (kBudget - kAccBytes - 512) / kStageBytes;
-    static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
-    static_assert(kStages >= 2, "shared-memory ring too small");
-    static constexpr int kAccOffset = kStages * kStageBytes;
-    static constexpr int kBarOffset = kAccOffset + kAccBytes;  // full[S], empty[S]
-    static constexpr int kFlagOffset = kBarOffset + 2 * kStages * 8;
-    // flags: abort (int), the flush's abort snapshot (int), the finish decision of each column
-    // block shared by its two warps (8 ints)
-    static constexpr int kNormOffset = kFlagOffset + 64;      // fused RMSNorm: 1/rms of each row
-    static constexpr int kTotal = kNormOffset + 4 * EXL3B_GEMV_MAX_ROWS;
+    static constexpr int kMaxStages = 8;
+    static constexpr int kTail = 2 * kMaxStages * 8 + 64 + 4 * EXL3B_GEMV_MAX_ROWS;  // barriers, flags, 1/rms
+    static_assert((kBudget - 8 * MT * kAccCols * 4 - kTail) / kStageBytes >= 2, "shared-memory ring too small");
 };
+
+// Runtime part of the layout (depends on m): ring, accumulator tile, then full[S], empty[S]
+// barriers; flags: abort (int), the flush's abort snapshot (int), the finish decision of each column
+// block shared by its two warps (8 ints); then the fused RMSNorm's 1/rms of each row.
+struct GemvLayout {
+    int stages, acc_off, bar_off, flag_off, norm_off, total;
+};
+template <int K, int MT, int R0>
+__host__ __device__ inline GemvLayout gemv_layout(int m) {
+    using S = GemvSmem<K, MT, R0>;
+    GemvLayout L;
+    const int acc = (m * kAccCols * 4 + 127) / 128 * 128;
+    L.stages = (S::kBudget - acc - S::kTail) / S::kStageBytes;
+    if (L.stages > S::kMaxStages) L.stages = S::kMaxStages;
+    L.acc_off = L.stages * S::kStageBytes;
+    L.bar_off = L.acc_off + acc;
+    L.flag_off = L.bar_off + 2 * L.stages * 8;
+    L.norm_off = L.flag_off + 64;
+    L.total = L.norm_off + 4 * EXL3B_GEMV_MAX_ROWS;
+    return L;
+}
 
 // Decode warps blk (half 0) and blk + 8 (half 1) finish column block `blk` of super-block `sb`
 // (only when a CTA leaves a super-block); with m > 1 each takes half of the rows, half 0 the first
@@ -381,20 +399,21 @@ EXL3B_DEV void norm_partials(const GemvParams& p, float* part, int warp, int lan
 template <int K, int CB, int MT, int R0_>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     using S = GemvSmem<K, MT, R0_>;
-    constexpr int kStages = S::kStages;
+    const GemvLayout lay = gemv_layout<K, MT, R0_>(p.m);
+    const int kStages = lay.stages;
     constexpr int R0 = S::R0;
     const int q = p.q, R = R0 * p.q;  // k-rows per unit; row r sits in slot r / q at tile (r % q) * 64 / q
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t full0 = sbase + S::kBarOffset, empty0 = full0 + kStages * 8;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kFlagOffset);
+    const uint32_t full0 = sbase + lay.bar_off, empty0 = full0 + kStages * 8;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + lay.flag_off);
     volatile int* flush_snap = abort_flag + 1;  // the abort flag as every flushing warp sees it
     volatile int* fin_s = abort_flag + 2;       // [8] finish decisions of the column-block pairs
-    float* inv_rms = reinterpret_cast<float*>(smem + S::kNormOffset);
+    float* inv_rms = reinterpret_cast<float*>(smem + lay.norm_off);
     // the fused RMSNorm's per-warp row sums borrow the accumulator tile: no flush can write it before
     // the producer has read them (the first flush follows the first published unit)
-    float* norm_part = reinterpret_cast<float*>(smem + S::kAccOffset);
+    float* norm_part = reinterpret_cast<float*>(smem + lay.acc_off);
 
     const int c = blockIdx.x, P = p.ctas, U = p.units, ku = p.ku, m = p.m;
     const int u0 = unit_start(c, U, P), u1 = unit_start(c + 1, U, P);
@@ -535,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         return;
     }
 
-    float* acc_s = reinterpret_cast<float*>(smem + S::kAccOffset);
+    float* acc_s = reinterpret_cast<float*>(smem + lay.acc_off);
 
     // ------------------------------ decode warps ------------------------------
     if (p.norm_w) {  // the fused RMSNorm's row sums, shared with the producer
@@ -707,6 +726,85 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------------------
+// decode ceiling: the GEMV's per-tile work (trellis words from shared memory, window extraction,
+// codebook decode into mma A fragments, one m16n8k16 per tile) with no HBM traffic and no stage
+// hand-offs, over one resident stage of 8 k-rows x 64 tiles, `iters` times.  It bounds the rate at
+// which this decode can feed the tensor core, in tiles per second.
+// ---------------------------------------------------------------------------------------------
+constexpr int kCeilRows = 8;
+template <int K, int CB>
+__global__ void __launch_bounds__(kDecodeWarps * 32, 1)
+decode_ceiling_kernel(const uint16_t* trellis, int iters, int zero, float* out) {
+    constexpr int kTile = 32 * K, kRowBytes = kSbTiles * kTile;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(trellis);
+        uint4* dst = reinterpret_cast<uint4*>(smem);
+        for (int i = threadIdx.x; i < kCeilRows * kRowBytes / 16; i += blockDim.x) dst[i] = src[i];
+        // B fragments (A_had of one k-tile, 8 rows): fp16 1/8
+        uint32_t* bf = reinterpret_cast<uint32_t*>(smem + kCeilRows * kRowBytes);
+        for (int i = threadIdx.x; i < kCeilRows * 64; i += blockDim.x) bf[i] = 0x30003000u;
+    }
+    __syncthreads();
+    LaneGeom<K> geom;
+    geom.init(lane);
+    uint32_t woff[LaneGeom<K>::kNW];
+#pragma unroll
+    for (int q = 0; q < LaneGeom<K>::kNW; ++q) woff[q] = (uint32_t)(warp * kTile) + geom.off[q];
+    const uint32_t boff = (uint32_t)(kCeilRows * kRowBytes + (lane >> 2) * 32 + (lane & 3) * 8);
+    float acc[4][4] = {};
+#pragma unroll 1
+    for (int it = 0; it < iters; ++it) {
+        // `zero` is 0 at run time; an offset the compiler cannot see through keeps every load (and
+        // the decode of what it loads) inside the loop, as in the GEMV, where each unit is new data
+        const uint8_t* st = smem + (uint32_t)(it & zero) * 16u;
+#pragma unroll
+        for (int r = 0; r < kCeilRows; ++r) {
+            const uint2 b = *reinterpret_cast<const uint2*>(st + boff + r * 256);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t Wd[LaneGeom<K>::kNW];
+#pragma unroll
+                for (int qq = 0; qq < LaneGeom<K>::kNW; ++qq)
+                    Wd[qq] = *reinterpret_cast<const uint32_t*>(st + woff[qq] + r * kRowBytes + j * 16 * kTile);
+                uint32_t a[4];
+                lane_decode_frag<K, CB>(Wd, geom.phi, a);
+                mma_16816_nv(acc[j], a, b.x, b.y);
+            }
+        }
+    }
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t += acc[j][0] + acc[j][1] + acc[j][2] + acc[j][3];
+    out[(blockIdx.x * kDecodeWarps + warp) * 32 + lane] = t;
+}
+
+template <int K, int CB>
+static cudaError_t launch_ceiling(const uint16_t* trellis, int iters, float* out, int ctas, cudaStream_t st) {
+    const int bytes = kCeilRows * kSbTiles * 32 * K + kCeilRows * 256;
+    auto kern = decode_ceiling_kernel<K, CB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    kern<<<ctas, kDecodeWarps * 32, bytes, st>>>(trellis, iters, 0, out);
+    return cudaGetLastError();
+}
+
+template <int CB>
+static cudaError_t launch_ceiling_k(int K, const uint16_t* trellis, int iters, float* out, int ctas, cudaStream_t st) {
+    switch (K) {
+        case 1: return launch_ceiling<1, CB>(trellis, iters, out, ctas, st);
+        case 2: return launch_ceiling<2, CB>(trellis, iters, out, ctas, st);
+        case 3: return launch_ceiling<3, CB>(trellis, iters, out, ctas, st);
+        case 4: return launch_ceiling<4, CB>(trellis, iters, out, ctas, st);
+        case 5: return launch_ceiling<5, CB>(trellis, iters, out, ctas, st);
+        case 6: return launch_ceiling<6, CB>(trellis, iters, out, ctas, st);
+        case 7: return launch_ceiling<7, CB>(trellis, iters, out, ctas, st);
+        default: return launch_ceiling<8, CB>(trellis, iters, out, ctas, st);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 constexpr size_t kHeaderBytes = 256;
@@ -820,14 +918,15 @@ static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st) {
     int dev = 0;
     cudaGetDevice(&dev);
     static cudaError_t attr_err[64];
-    std::call_once(once[dev & 63], [&] {
-        attr_err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    std::call_once(once[dev & 63], [&] {  // the budget covers every m
+        attr_err[dev & 63] =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBudget);
     });
     if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.ctas);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = S::kTotal;
+    cfg.dynamicSmemBytes = gemv_layout<K, MT, R0>(p.m).total;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -839,12 +938,13 @@ static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st) {
 
 template <int CB, int MT>
 static cudaError_t launch_gemv_k(int K, int r0, const GemvParams& p, cudaStream_t st) {
-    const bool r2 = r0 == 2;  // K <= 4 has units of 8 or 2 rows per slot, K > 4 of 2
+    const bool r2 = r0 == 2;  // K <= 4 has units of kR0SmallK or 2 rows per slot, K > 4 of 2
+    constexpr int RS = kR0SmallK;
     switch (K) {
-        case 1: return r2 ? launch_gemv<1, CB, MT, 2>(p, st) : launch_gemv<1, CB, MT, 8>(p, st);
-        case 2: return r2 ? launch_gemv<2, CB, MT, 2>(p, st) : launch_gemv<2, CB, MT, 8>(p, st);
-        case 3: return r2 ? launch_gemv<3, CB, MT, 2>(p, st) : launch_gemv<3, CB, MT, 8>(p, st);
-        case 4: return r2 ? launch_gemv<4, CB, MT, 2>(p, st) : launch_gemv<4, CB, MT, 8>(p, st);
+        case 1: return r2 ? launch_gemv<1, CB, MT, 2>(p, st) : launch_gemv<1, CB, MT, RS>(p, st);
+        case 2: return r2 ? launch_gemv<2, CB, MT, 2>(p, st) : launch_gemv<2, CB, MT, RS>(p, st);
+        case 3: return r2 ? launch_gemv<3, CB, MT, 2>(p, st) : launch_gemv<3, CB, MT, RS>(p, st);
+        case 4: return r2 ? launch_gemv<4, CB, MT, 2>(p, st) : launch_gemv<4, CB, MT, RS>(p, st);
         case 5: return launch_gemv<5, CB, MT, 2>(p, st);
         case 6: return launch_gemv<6, CB, MT, 2>(p, st);
         case 7: return launch_gemv<7, CB, MT, 2>(p, st);
@@ -1074,5 +1174,20 @@ extern "C" int exl3b_linear_workspace_error(const void* workspace, int* out, voi
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e = cudaMemcpyAsync(out, workspace, sizeof(int), cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return cuda_status(e);
+}
+
+extern "C" int exl3b_decode_ceiling(int K, int codebook, const uint16_t* trellis, int iters, float* out,
+                                    int* ctas, void* stream) {
+    if (K < 1 || K > 8 || codebook < 0 || codebook > 2 || iters < 1) return EXL3B_DECLINED;
+    if (!trellis || !out || !ctas || !aligned(trellis, 16) || !aligned(out, 4)) return EXL3B_BAD_ARG;
+    *ctas = num_sms();
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    switch (codebook) {
+        case 0: e = launch_ceiling_k<0>(K, trellis, iters, out, *ctas, st); break;
+        case 1: e = launch_ceiling_k<1>(K, trellis, iters, out, *ctas, st); break;
+        default: e = launch_ceiling_k<2>(K, trellis, iters, out, *ctas, st); break;
+    }
     return cuda_status(e);
 }
