@@ -42,7 +42,9 @@ constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summ
 constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
 constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
 
-// trellis k-tile slots per unit (64 tiles each) at K <= 4; K > 4 takes 2.
+// trellis k-tile slots per unit (64 tiles each) at K <= 4; K > 4 takes 2.  Larger units measured
+// faster: at K = 4, units of 4 slots made the layer step 10 % slower and units of 2 40 % slower
+// than units of 8 (fewer hand-offs between producer and decode warps per byte).
 #ifndef EXL3B_GEMV_R0_SMALLK
 #define EXL3B_GEMV_R0_SMALLK 8
 #endif
@@ -138,8 +140,9 @@ EXL3B_DEV SbInfo sb_info(const GemvGroups& gg, int groups, int sb) {
 // ---------------------------------------------------------------------------------------------
 // Shared memory: a ring of `stages` stages (R trellis rows of up to 64 tiles at a fixed stride,
 // then the unit's A_had rows), the fp32 accumulator tile [m rows][kAccCols] where the decode
-// warps pool a finished super-block, and the mbarriers.  The stage size is fixed by K, MT and R0;
-// the tile has one row per input row, so that few rows leave room for a deeper ring.
+// warps pool a finished super-block, and the mbarriers.  The ring depth is what the budget leaves
+// beside a tile of 8 MT rows, whatever m: at m = 1 a third 64 KB stage (room for it exists) measured
+// 3 % slower per layer step, its copies in flight competing with the next unit's.
 template <int K, int MT, int R0_>
 struct GemvSmem {
     static constexpr int R0 = R0_;                         // stage slots of 64 tiles
@@ -165,7 +168,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int m) {
     using S = GemvSmem<K, MT, R0>;
     GemvLayout L;
     const int acc = (m * kAccCols * 4 + 127) / 128 * 128;
-    L.stages = (S::kBudget - acc - S::kTail) / S::kStageBytes;
+    L.stages = (S::kBudget - 8 * MT * kAccCols * 4 - S::kTail) / S::kStageBytes;
     if (L.stages > S::kMaxStages) L.stages = S::kMaxStages;
     L.acc_off = L.stages * S::kStageBytes;
     L.bar_off = L.acc_off + acc;
