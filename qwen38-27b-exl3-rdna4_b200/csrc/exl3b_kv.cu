@@ -192,43 +192,6 @@ struct KvInt4Extra {
     __half* exact_k; __half* exact_v; int32_t* exact_tag;  // per slot [kExactRows][H][128], [kExactRows]
 };
 
-EXL3B_DEV int round_half_away(float v) { return __float2int_rz(v >= 0.f ? __fadd_rn(v, 0.5f) : __fsub_rn(v, 0.5f)); }
-
-// codes c[4] (0..15) for this lane's 4 elements and the row's scale bits
-EXL3B_DEV void int4_quant_row(const float (&y)[4], int (&code)[4], uint32_t& sbits) {
-    const float lo0 = warp_min(fminf(fminf(y[0], y[1]), fminf(y[2], y[3])));
-    const float hi0 = warp_max(fmaxf(fmaxf(y[0], y[1]), fmaxf(y[2], y[3])));
-    const float mu = __fmul_rn(warp_sum(__fadd_rn(__fadd_rn(__fadd_rn(y[0], y[1]), y[2]), y[3])), 1.f / 128.f);
-    float best_err = __int_as_float(0x7F800000), best_sc = 0.f;
-    int best_zp = 0;
-#pragma unroll 1
-    for (int c = 0; c < kClipSteps * kClipSteps; ++c) {
-        const float flo = __fmaf_rn(-kClipStep, (float)(c / kClipSteps), 1.f);
-        const float fhi = __fmaf_rn(-kClipStep, (float)(c % kClipSteps), 1.f);
-        const float lo = __fmaf_rn(__fsub_rn(lo0, mu), flo, mu);
-        const float hi = __fmaf_rn(__fsub_rn(hi0, mu), fhi, mu);
-        const float sc = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 15.f), 1e-6f);
-        const int zp = min(max(round_half_away(__fdiv_rn(-lo, sc)), 0), 15);
-        const float inv = __fdiv_rn(1.f, sc);
-        float e[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int qn = min(max(round_half_away(__fmaf_rn(y[i], inv, (float)zp)), 0), 15);
-            e[i] = __fmaf_rn((float)(qn - zp), sc, -y[i]);
-        }
-        float s = __fmul_rn(e[0], e[0]);
-        s = __fmaf_rn(e[1], e[1], s);
-        s = __fmaf_rn(e[2], e[2], s);
-        s = __fmaf_rn(e[3], e[3], s);
-        const float err = warp_sum(s);
-        if (err < best_err) { best_err = err; best_sc = sc; best_zp = zp; }
-    }
-    const float inv = __fdiv_rn(1.f, best_sc);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) code[i] = min(max(round_half_away(__fmaf_rn(y[i], inv, (float)best_zp)), 0), 15);
-    sbits = ((uint32_t)__float_as_uint(best_sc) & 0xFFFFFFF0u) | (uint32_t)best_zp;
-}
-
 // sequence of token t from query_start_loc (binary search, as vLLM's find_seq_idx)
 EXL3B_DEV int seq_of_token(const int32_t* qsl, int num_seqs, int t) {
     int lo = 0, hi = num_seqs;
@@ -241,34 +204,161 @@ EXL3B_DEV int seq_of_token(const int32_t* qsl, int num_seqs, int t) {
 
 EXL3B_DEV int exact_row(int pos) { return pos < kSinks ? pos : kSinks + pos % kTail; }
 
-__global__ void kv_int4_write_kernel(const KvWriteArgs a, const KvInt4Extra x) {
-    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (item >= (int64_t)a.num_tokens * a.num_heads * 2) return;
-    const int lane = threadIdx.x & 31;
+// One warp per eight rows (token, KV head, side), four lanes per row.  Lane j of a row holds the
+// 4-element chunks l = j + 4i (i = 0..7) of its 128 elements: the unnormalised Hadamard (H4 inside a
+// chunk, then butterflies over chunk distances 1, 2, 4, 8, 16), the row sums and the clip search's
+// error sums then run in exactly the order of a warp holding chunk l in lane l (distances 16, 8 and
+// 4 fall inside a lane, 2 and 1 between the row's lanes), so the codes and scales are bit for bit
+// those of the oracle, while a warp shuffles twice per sum instead of five times and keeps all of
+// its lanes on useful work (a warp per row issued ~1500 instructions per row).
+constexpr int kW4Rows = 8;  // rows per warp
+EXL3B_DEV float sum_chunks(const float (&c)[8]) {  // the xor-16/8/4 levels over this lane's chunks
+    const float t0 = __fadd_rn(c[0], c[4]), t1 = __fadd_rn(c[1], c[5]), t2 = __fadd_rn(c[2], c[6]),
+                t3 = __fadd_rn(c[3], c[7]);
+    return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+}
+EXL3B_DEV float row_sum4(float v) {  // the xor-2/1 levels between the row's four lanes
+    v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+    return __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+}
+// round_half_away(v) clamped to [0, 15], as a float: for v >= 0 it is floor(v + 0.5), and negative v
+// (whose rounding is <= 0) clamps to 0 either way
+EXL3B_DEV float code_of(float v) { return fminf(fmaxf(floorf(__fadd_rn(v, 0.5f)), 0.f), 15.f); }
+
+__global__ void __launch_bounds__(256) kv_int4_write_kernel(const KvWriteArgs a, const KvInt4Extra x) {
+    const int lane = threadIdx.x & 31, j = lane & 3;
+    const int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kW4Rows + (lane >> 2);
+    const int64_t items = (int64_t)a.num_tokens * a.num_heads * 2;
+    // rows outside the call or without a slot run along on zeros (every lane takes part in the shuffles)
+    bool live = item < items;
     const int side = (int)(item & 1);
-    const int t = (int)((item >> 1) / a.num_heads), h = (int)((item >> 1) % a.num_heads);
-    const int64_t slot = a.slot_mapping[t];
-    if (slot < 0) return;
+    const int t = live ? (int)((item >> 1) / a.num_heads) : 0, h = live ? (int)((item >> 1) % a.num_heads) : 0;
+    const int64_t slot = live ? a.slot_mapping[t] : -1;
+    live = live && slot >= 0;
     const void* src = side ? a.value : a.key;
     const int64_t base = side ? t * a.v_stride_tok + h * a.v_stride_head : t * a.k_stride_tok + h * a.k_stride_head;
-    float v[4];
+    const bool vec = ((base & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 7) == 0);
+    float y[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = load_in(src, base + 4 * lane + i, a.dtype) * x.signs[4 * lane + i];
-    // unnormalised Hadamard, fp32, H4 in lane then xor butterflies 1..16 (same order as had128_warp)
-    had128_warp(v);
+    for (int i = 0; i < 8; ++i) {
+        const int e0 = 16 * i + 4 * j;
+        const float4 sg = *reinterpret_cast<const float4*>(x.signs + e0);
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+            if (vec) {
+                const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(src) + base + e0);
+                if (a.dtype == 0) {
+                    v[0] = __low2float(u32_as_h2(w.x)); v[1] = __high2float(u32_as_h2(w.x));
+                    v[2] = __low2float(u32_as_h2(w.y)); v[3] = __high2float(u32_as_h2(w.y));
+                } else {
+                    v[0] = __uint_as_float(w.x << 16); v[1] = __uint_as_float(w.x & 0xFFFF0000u);
+                    v[2] = __uint_as_float(w.y << 16); v[3] = __uint_as_float(w.y & 0xFFFF0000u);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) v[c] = load_in(src, base + e0 + c, a.dtype);
+            }
+        }
+        y[i][0] = v[0] * sg.x; y[i][1] = v[1] * sg.y; y[i][2] = v[2] * sg.z; y[i][3] = v[3] * sg.w;
+        // H4 inside the chunk
+        const float s0 = y[i][0] + y[i][1], d0 = y[i][0] - y[i][1];
+        const float s1 = y[i][2] + y[i][3], d1 = y[i][2] - y[i][3];
+        y[i][0] = s0 + s1; y[i][1] = d0 + d1; y[i][2] = s0 - s1; y[i][3] = d0 - d1;
+    }
+    // chunk distances 1 and 2: the partner chunk is in lane j ^ 1 / j ^ 2 (lower chunk: own + partner,
+    // upper chunk: partner - own)
+#pragma unroll
+    for (int d = 1; d <= 2; d <<= 1) {
+        const bool upper = (j & d) != 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float o = __shfl_xor_sync(0xFFFFFFFFu, y[i][c], d);
+                y[i][c] = upper ? (o - y[i][c]) : (y[i][c] + o);
+            }
+    }
+    // chunk distances 4, 8, 16: i ^ 1, i ^ 2, i ^ 4 inside the lane
+#pragma unroll
+    for (int d = 1; d <= 4; d <<= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (!(i & d))
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float lo = y[i][c], hi = y[i | d][c];
+                    y[i][c] = lo + hi;
+                    y[i | d][c] = lo - hi;
+                }
     const float* bias = side ? x.bias_v : x.bias_k;
     if (bias) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = __fadd_rn(v[i], bias[h * kHD + 4 * lane + i]);
+        for (int i = 0; i < 8; ++i) {
+            const float4 b = *reinterpret_cast<const float4*>(bias + h * kHD + 16 * i + 4 * j);
+            y[i][0] = __fadd_rn(y[i][0], b.x); y[i][1] = __fadd_rn(y[i][1], b.y);
+            y[i][2] = __fadd_rn(y[i][2], b.z); y[i][3] = __fadd_rn(y[i][3], b.w);
+        }
     }
-    int code[4];
-    uint32_t sbits;
-    int4_quant_row(v, code, sbits);
+    // ---- 3x3 clip search (kv_int4.py:198-213), the row-wide sums in the order described above ----
+    float lo0 = y[0][0], hi0 = y[0][0];
+    float cs[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        lo0 = fminf(lo0, fminf(fminf(y[i][0], y[i][1]), fminf(y[i][2], y[i][3])));
+        hi0 = fmaxf(hi0, fmaxf(fmaxf(y[i][0], y[i][1]), fmaxf(y[i][2], y[i][3])));
+        cs[i] = __fadd_rn(__fadd_rn(__fadd_rn(y[i][0], y[i][1]), y[i][2]), y[i][3]);
+    }
+#pragma unroll
+    for (int d = 2; d >= 1; d >>= 1) {
+        lo0 = fminf(lo0, __shfl_xor_sync(0xFFFFFFFFu, lo0, d));
+        hi0 = fmaxf(hi0, __shfl_xor_sync(0xFFFFFFFFu, hi0, d));
+    }
+    const float mu = __fmul_rn(row_sum4(sum_chunks(cs)), 1.f / 128.f);
+    float ny[8][4];  // -y, the addend of every candidate's error
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ny[i][c] = -y[i][c];
+    float best_err = __int_as_float(0x7F800000), best_sc = 0.f, best_zp = 0.f;
+#pragma unroll 1
+    for (int cand = 0; cand < kClipSteps * kClipSteps; ++cand) {
+        const float flo = __fmaf_rn(-kClipStep, (float)(cand / kClipSteps), 1.f);
+        const float fhi = __fmaf_rn(-kClipStep, (float)(cand % kClipSteps), 1.f);
+        const float lo = __fmaf_rn(__fsub_rn(lo0, mu), flo, mu);
+        const float hi = __fmaf_rn(__fsub_rn(hi0, mu), fhi, mu);
+        const float sc = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 15.f), 1e-6f);
+        const float zp = code_of(__fdiv_rn(-lo, sc));
+        const float inv = __fdiv_rn(1.f, sc);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float e[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                e[c] = __fmaf_rn(code_of(__fmaf_rn(y[i][c], inv, zp)) - zp, sc, ny[i][c]);
+            float q = __fmul_rn(e[0], e[0]);
+            q = __fmaf_rn(e[1], e[1], q);
+            q = __fmaf_rn(e[2], e[2], q);
+            cs[i] = __fmaf_rn(e[3], e[3], q);
+        }
+        const float err = row_sum4(sum_chunks(cs));
+        if (err < best_err) { best_err = err; best_sc = sc; best_zp = zp; }
+    }
+    if (!live) return;  // no shuffles below
+    const float inv = __fdiv_rn(1.f, best_sc);
     const int64_t blk = slot / a.block_size, off = slot % a.block_size;
-    uint8_t* cache = reinterpret_cast<uint8_t*>(side ? a.value_cache : a.key_cache) + a.lay.row(blk, off, h);
-    const uint16_t packed = (uint16_t)((code[0] | (code[1] << 4)) | ((code[2] | (code[3] << 4)) << 8));
-    reinterpret_cast<uint16_t*>(cache)[lane] = packed;
-    if (lane == 0) (side ? a.v_scale : a.k_scale)[a.lay.srow(blk, off, h)] = __uint_as_float(sbits);
+    uint16_t* cache = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(side ? a.value_cache : a.key_cache) +
+                                                  a.lay.row(blk, off, h));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        int code[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) code[c] = (int)code_of(__fmaf_rn(y[i][c], inv, best_zp));
+        cache[j + 4 * i] = (uint16_t)((code[0] | (code[1] << 4)) | ((code[2] | (code[3] << 4)) << 8));
+    }
+    if (j == 0) {
+        const uint32_t sbits = ((uint32_t)__float_as_uint(best_sc) & 0xFFFFFFF0u) | (uint32_t)best_zp;
+        (side ? a.v_scale : a.k_scale)[a.lay.srow(blk, off, h)] = __uint_as_float(sbits);
+    }
     // exact rows
     if (x.exact_tag && x.seq_slots) {
         const int s = seq_of_token(x.query_start_loc, x.num_seqs, t);
@@ -279,9 +369,12 @@ __global__ void kv_int4_write_kernel(const KvWriteArgs a, const KvInt4Extra x) {
         if (rs >= 0 && pos >= 0 && (pos < kSinks || pos >= L - kTail)) {
             const int e = exact_row(pos);
             __half* ex = (side ? x.exact_v : x.exact_k) + (((int64_t)rs * kExactRows + e) * a.num_heads + h) * kHD;
-            reinterpret_cast<uint2*>(ex)[lane] = make_uint2(h2_as_u32(__floats2half2_rn(v[0], v[1])),
-                                                           h2_as_u32(__floats2half2_rn(v[2], v[3])));
-            if (side == 0 && h == 0 && lane == 0) x.exact_tag[(int64_t)rs * kExactRows + e] = pos;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                *reinterpret_cast<uint2*>(ex + 16 * i + 4 * j) =
+                    make_uint2(h2_as_u32(__floats2half2_rn(y[i][0], y[i][1])),
+                               h2_as_u32(__floats2half2_rn(y[i][2], y[i][3])));
+            if (side == 0 && h == 0 && j == 0) x.exact_tag[(int64_t)rs * kExactRows + e] = pos;
         }
     }
 }
@@ -369,12 +462,21 @@ struct KvTraits<4> {
 
 // Per-warp shared memory: a ring of kRing tiles (32 tokens: K rows, V rows, k scales, v scales)
 // filled with cp.async one tile ahead of the math, and a window of the split's block ids.
+// Occupancy of the split-KV kernels (one warp per CTA for decode).  int8: a two-tile ring (17.9 KB a
+// warp) lets a B200 SM hold 12 CTAs, and the one-n-tile kernel is held to 168 registers so that 12 fit
+// (187 unbounded measured 3277 against 4257 GB/s at 32k x 8: 10 resident warps and a second wave).
+// int4: a two-tile ring (9.7 KB a warp) and 128 registers make 16 resident warps per SM; against
+// three tiles and 12 warps, 32k x 8 went 1639 -> 1948 GB/s and 64k x 8 1901 -> 2136 GB/s.
+constexpr int kRing4 = 2;
+constexpr int kWarpsPerSm8 = 12, kWarpsPerSm4 = 16;
+template <int KV, int NT>
+constexpr int attn_min_blocks() { return NT > 1 ? 1 : KV == 4 ? 4 : 3; }
 template <int KV>
 struct AttnSmem {
     static constexpr int kRowBytes = KV == 8 ? kHD : kHD / 2;
     static constexpr int kRows = 32 * kRowBytes;                  // K (or V) bytes of one tile
     static constexpr int kTile = 2 * kRows + 2 * 32 * 4;          // K, V, k scales, v scales
-    static constexpr int kRing = KV == 8 ? 2 : 3;
+    static constexpr int kRing = KV == 8 ? 2 : kRing4;
     static constexpr int kBtWindow = 256;                          // block ids kept per warp
     static constexpr int kWarpBytes = kRing * kTile + kBtWindow * 4;
 };
@@ -421,7 +523,7 @@ EXL3B_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_pe
 // reads 16 contiguous bytes (int8) or 8 (int4) of each of its 4 tokens per 16-token chunk.
 // Each warp owns 8 * NT query rows; the CTA's warps share nothing and never wait on one another.
 template <int KV, int NT>
-__global__ void __launch_bounds__(32 * 4) kv_attn_kernel(const KvAttnArgs a) {
+__global__ void __launch_bounds__(32 * 4, attn_min_blocks<KV, NT>()) kv_attn_kernel(const KvAttnArgs a) {
     griddep_launch();  // the split combine may be scheduled now; it waits for this grid's partials
     griddep_wait();    // a programmatic dependent launch: q and the cache rows come from earlier kernels
     using Tr = KvTraits<KV>;
@@ -869,11 +971,11 @@ __global__ void __launch_bounds__(32 * 4) kv_attn_kernel(const KvAttnArgs a) {
             l_i[nt][h] = l;
         }
 
-    if (ts > 1) {
+    if (NT == 1 && ts > 1) {  // the host shares a split among warps only when one n-tile holds all rows
         // merge the warps' (m, l, acc) of the same rows: each warp parks its values in its own ring
         // area (field-major, conflict-free), then warp 0 combines them with weights 2^(m_w - M)
         constexpr int kF = NT * 36;  // acc 32 + m 2 + l 2 per n-tile
-        static_assert(kF * 32 * 4 <= AttnSmem<KV>::kWarpBytes, "merge area");
+        static_assert(NT > 1 || kF * 32 * 4 <= AttnSmem<KV>::kWarpBytes, "merge area");
         float* park = reinterpret_cast<float*>(wsm);
         __syncwarp();
 #pragma unroll
@@ -1127,9 +1229,13 @@ static int kv_num_sms() {
 // run as a second, almost empty wave).  A split must stream enough keys to pay for its start-up:
 // 128 for up to 8 query rows per KV head (decode), 256 above (speculative verify).  rows = 1
 // gives the most splits any call of the shape can take (the workspace bound).
-static int kv_splits(int num_seqs, int num_kv_heads, int max_seq_len, int rows, int ts = 1) {
-    const int want = (12 * kv_num_sms()) / (num_seqs * num_kv_heads * ts);
-    const int min_keys = (rows <= 8 ? 128 : 256) * ts;  // per warp: ts warps share a split
+// Splits per (sequence, KV head): enough one-warp CTAs to fill the SMs in one wave (the resident
+// warps above), each split at least min_keys long per warp.  int4 decode splits keep >= 160 keys: at
+// 4k x 8, 32 splits of 128 keys measured 553 GB/s against 683 for 27 of 152 (the per-split set-up and
+// partial dominate such short splits).
+static int kv_splits(int kv, int num_seqs, int num_kv_heads, int max_seq_len, int rows, int ts = 1) {
+    const int want = ((kv == 4 ? kWarpsPerSm4 : kWarpsPerSm8) * kv_num_sms()) / (num_seqs * num_kv_heads * ts);
+    const int min_keys = (rows <= 8 ? (kv == 4 ? 160 : 128) : 256) * ts;  // per warp: ts warps share a split
     const int by_len = (max_seq_len + min_keys - 1) / min_keys;
     return std::max(1, std::min(kMaxSplits, std::min(want, by_len)));
 }
@@ -1147,6 +1253,9 @@ static cudaError_t launch_attn(dim3 grid, int warps, const KvAttnArgs& a, cudaSt
     cudaGetDevice(&dev);
     std::call_once(once[dev & 63], [&] {
         attr_err[dev & 63] = cudaFuncSetAttribute(kv_attn_kernel<KV, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (attr_err[dev & 63] == cudaSuccess)  // all of the unified L1 as shared memory: most resident CTAs
+            attr_err[dev & 63] =
+                cudaFuncSetAttribute(kv_attn_kernel<KV, NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     });
     if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
     cudaLaunchConfig_t cfg = {};
@@ -1289,14 +1398,16 @@ extern "C" int exl3b_kv_int4_write(const void* key, const void* value, int dtype
     x.exact_k = reinterpret_cast<__half*>(exact_k); x.exact_v = reinterpret_cast<__half*>(exact_v);
     x.exact_tag = exact_tag;
     const int64_t items = num_tokens * num_kv_heads * 2;
-    kv_int4_write_kernel<<<(unsigned)((items + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a, x);
+    const int64_t per_block = 8 * kW4Rows;  // 8 warps of kW4Rows rows
+    kv_int4_write_kernel<<<(unsigned)((items + per_block - 1) / per_block), 256, 0, (cudaStream_t)stream>>>(a, x);
     return cuda_status(cudaGetLastError());
 }
 
 extern "C" size_t exl3b_kv_attn_workspace_bytes(int num_tokens, int num_q_heads, int num_seqs, int num_kv_heads,
                                                 int max_seq_len) {
     if (num_tokens <= 0 || num_q_heads <= 0 || num_seqs <= 0 || num_kv_heads <= 0) return 0;
-    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len), 1);
+    const int S = std::max(kv_splits(8, num_seqs, num_kv_heads, std::max(1, max_seq_len), 1),
+                           kv_splits(4, num_seqs, num_kv_heads, std::max(1, max_seq_len), 1));
     const size_t qr = (size_t)num_tokens * num_q_heads * kHD * 2;
     return (qr + 255) / 256 * 256 + (size_t)num_tokens * num_q_heads * S * kPartialStride * 4;
 }
@@ -1326,7 +1437,7 @@ static int kv_attn_common(int kv, const uint16_t* q, uint16_t* out, int num_toke
     // combine has as many times fewer partials (measured: int4 64k x 1 72.7 -> 58.2 us; int8 and
     // batched decode measured the same or slower, so they keep one warp per split)
     const int ts = (kv == 4 && max_q_len * G <= 8 && num_seqs * num_kv_heads <= 16) ? kDecodeTsplit : 1;
-    const int S = kv_splits(num_seqs, num_kv_heads, std::max(1, max_seq_len), max_q_len * G, ts);
+    const int S = kv_splits(kv, num_seqs, num_kv_heads, std::max(1, max_seq_len), max_q_len * G, ts);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const size_t qr_bytes = ((size_t)num_tokens * num_q_heads * kHD * 2 + 255) / 256 * 256;
     const __half* qin = reinterpret_cast<const __half*>(q);
