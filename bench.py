@@ -705,7 +705,7 @@ def main():
                     help="comma list of the layer's modules a step runs (default: all four)")
     ap.add_argument("--only", default=None,
                     help="run one leg alone and print its record (for profiler captures): "
-                         "kv:<8|4>:<ctx>:<batch>:<q_len>, kv_write:<8|4>:<tokens>, ceiling:<K>")
+                         "kv:<8|4>:<ctx>:<batch>:<q_len>, kv_write:<8|4>:<tokens>, ceiling:<K>, prefill:<K>[:<m>]")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
     if args.only:
@@ -721,6 +721,8 @@ def main():
             rec = bench_kv_write(torch, dev, *map(int, a), iters=args.steps)
         elif kind == "ceiling":
             rec = bench_decode_ceiling(torch, dev, int(a[0]), reps=args.steps)
+        elif kind == "prefill":
+            rec = bench_prefill(torch, dev, int(a[0]), m=int(a[1]) if len(a) > 1 else 2048, iters=args.steps)
         else:
             raise SystemExit(f"unknown leg {kind}")
         print(json.dumps({"only": args.only, **rec}))
