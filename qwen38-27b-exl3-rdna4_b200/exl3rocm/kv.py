@@ -385,15 +385,16 @@ def _sdpa_paged(q, kd, vd, cu_seqlens_q, seqused_k, nb, softmax_scale, out):
         else:
             mask = torch.arange(L, device=q.device)[None, :] <= (L - ql + torch.arange(ql, device=q.device))[:, None]
             causal = False
-        # the KV heads repeated for their query heads: SDPA's fused kernels take equal head counts
-        # (enable_gqa sent an 8192-token prompt to the unfused path: 63 ms per layer)
+        # SDPA's fused kernels take 4-d [batch, heads, len, dim] inputs with equal head counts (3-d
+        # inputs ran its unfused fp32 path: 59 ms per layer for an 8192-token prompt): the KV heads
+        # are repeated for their query heads
         G = q.shape[1] // k.shape[1]
         if G > 1:
             k, v = k.repeat_interleave(G, dim=1), v.repeat_interleave(G, dim=1)
         o = torch.nn.functional.scaled_dot_product_attention(
-            q[q0:q1].transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), attn_mask=mask, is_causal=causal,
-            scale=softmax_scale)
-        out[q0:q1] = o.transpose(0, 1).to(out.dtype)
+            q[q0:q1].transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0), v.transpose(0, 1).unsqueeze(0),
+            attn_mask=mask, is_causal=causal, scale=softmax_scale)
+        out[q0:q1] = o[0].transpose(0, 1).to(out.dtype)
 
 
 def prefill(orig=None, kw=None, layer_name=None):
