@@ -38,7 +38,7 @@ constexpr int kThreads = (kDecodeWarps + 1) * 32;
 constexpr int kFlushBar = 1;      // named barrier of the decode warps
 constexpr int kNormBar = 2;       // named barrier of all warps after the fused RMSNorm's row sums
 constexpr int kPairBar0 = 3;      // named barriers 3..10: the two warps that finish column block b
-constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summing them
+constexpr int kMaxBatch = 4;      // partials a finishing warp loads before summing them (8 spilled 1.2 KB)
 constexpr int kSbTiles = 64;                 // n-tiles of a full super-block (1024 columns)
 constexpr int kAccCols = kSbTiles * 16 + 4;  // accumulator-tile row, padded against bank conflicts
 
@@ -734,7 +734,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 // hand-offs, over one resident stage of 8 k-rows x 64 tiles, `iters` times.  It bounds the rate at
 // which this decode can feed the tensor core, in tiles per second.
 // ---------------------------------------------------------------------------------------------
-constexpr int kCeilRows = 8;
+#ifndef EXL3B_CEIL_ROWS
+#define EXL3B_CEIL_ROWS 8
+#endif
+#ifndef EXL3B_CEIL_CTAS_PER_SM
+#define EXL3B_CEIL_CTAS_PER_SM 1
+#endif
+constexpr int kCeilRows = EXL3B_CEIL_ROWS;  // k-rows of the resident stage (the GEMV's units: 8)
 template <int K, int CB>
 __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
 decode_ceiling_kernel(const uint16_t* trellis, int iters, int zero, float* out) {
@@ -1184,7 +1190,7 @@ extern "C" int exl3b_decode_ceiling(int K, int codebook, const uint16_t* trellis
                                     int* ctas, void* stream) {
     if (K < 1 || K > 8 || codebook < 0 || codebook > 2 || iters < 1) return EXL3B_DECLINED;
     if (!trellis || !out || !ctas || !aligned(trellis, 16) || !aligned(out, 4)) return EXL3B_BAD_ARG;
-    *ctas = num_sms();
+    *ctas = num_sms() * EXL3B_CEIL_CTAS_PER_SM;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e;
     switch (codebook) {
