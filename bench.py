@@ -157,24 +157,29 @@ def run_layer(torch, layer, x, inputs, K, tp, pg, comm=None):
     row-parallel o and down read their own (sharded) inputs.  Under tensor parallelism o and down
     reduce across ranks inside their kernel (comm), or with an NCCL all-reduce after it (no comm).
     Returns the last output."""
-    ops = torch.ops.exl3rocm
     y = None
     for mod, names in MODULES:
-        ts = [layer[nm][0] for nm in names]
-        su = [layer[nm][1] for nm in names]
-        sv = [layer[nm][2] for nm in names]
-        kin = layer[names[0]][3]
-        xin = x if kin == x.shape[1] and mod in ("qkv", "gate_up") else inputs[kin]
-        if tp > 1 and mod in ("o", "down") and comm is not None:
-            from exl3rocm.tp import linear_tp
-            y = linear_tp(xin, ts[0], su[0], sv[0], K, False, True, comm)
-            continue
-        if len(names) == 1:
-            y = ops.linear(xin, ts[0], su[0], sv[0], K, False, True)
-        else:
-            y = ops.linear_groups(xin, ts, su, sv, [K] * len(names), False, True)
-        if tp > 1 and mod in ("o", "down"):
-            torch.distributed.all_reduce(y, group=pg)
+        y = run_module(torch, layer, mod, names, x, inputs, K, tp, pg, comm)
+    return y
+
+
+def run_module(torch, layer, mod, names, x, inputs, K, tp, pg, comm=None):
+    """One module of run_layer (qkv, o, gate_up or down); returns its output."""
+    ops = torch.ops.exl3rocm
+    ts = [layer[nm][0] for nm in names]
+    su = [layer[nm][1] for nm in names]
+    sv = [layer[nm][2] for nm in names]
+    kin = layer[names[0]][3]
+    xin = x if kin == x.shape[1] and mod in ("qkv", "gate_up") else inputs[kin]
+    if tp > 1 and mod in ("o", "down") and comm is not None:
+        from exl3rocm.tp import linear_tp
+        return linear_tp(xin, ts[0], su[0], sv[0], K, False, True, comm)
+    if len(names) == 1:
+        y = ops.linear(xin, ts[0], su[0], sv[0], K, False, True)
+    else:
+        y = ops.linear_groups(xin, ts, su, sv, [K] * len(names), False, True)
+    if tp > 1 and mod in ("o", "down"):
+        torch.distributed.all_reduce(y, group=pg)
     return y
 
 
@@ -802,16 +807,16 @@ def main():
             with torch.cuda.graph(g_, stream=stream):
                 outs.append(run_layer(torch, lay, x, inputs, K, world, pg, comm))
             graphs.append(g_)
-        # gate_up alone, for the per-call roofline of the dominant kernel
-        gu_graphs = []
-        for lay in layers:
-            ts = [lay[nm][0] for nm in ("gate", "up")]
-            su = [lay[nm][1] for nm in ("gate", "up")]
-            sv = [lay[nm][2] for nm in ("gate", "up")]
-            g_ = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_, stream=stream):
-                torch.ops.exl3rocm.linear_groups(x, ts, su, sv, [K, K], False, True)
-            gu_graphs.append(g_)
+        # each module alone, for the per-call roofline of the dominant kernel (gate_up) and the
+        # per-module times that name the step's limiting kernel
+        mod_graphs = {}
+        for mod, names in MODULES:
+            mod_graphs[mod] = []
+            for lay in layers:
+                g_ = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g_, stream=stream):
+                    run_module(torch, lay, mod, names, x, inputs, K, world, pg, comm)
+                mod_graphs[mod].append(g_)
     torch.cuda.synchronize()
 
     def barrier():
@@ -853,20 +858,35 @@ def main():
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
     clocks = clk.summary()
 
-    # ---- per-call timing of the dominant kernel's call (gate_up, the largest), graph-replayed ----
+    # ---- per-call timing of each module, graph-replayed (every rank replays the same calls) ----
     lay = layers[0]
     n_calls = 3 * copies
-    gu_ms = []
-    with torch.cuda.stream(stream):
-        for i in range(n_calls):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            gu_graphs[i % copies].replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            gu_ms.append(e0.elapsed_time(e1))
+    mod_ms = {}
+    for mod, _ in MODULES:
+        ms_l = []
+        with torch.cuda.stream(stream):
+            for i in range(n_calls):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                mod_graphs[mod][i % copies].replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                ms_l.append(e0.elapsed_time(e1))
+        mod_ms[mod] = statistics.median(ms_l)
+    if world > 1:  # the slowest rank's median per module
+        t = torch.tensor([mod_ms[m_] for m_, _ in MODULES], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        mod_ms = {m_: float(v) for (m_, _), v in zip(MODULES, t.tolist())}
+    limiting = max(mod_ms, key=mod_ms.get)
+    modules_line = {"us": {m_: v * 1000 for m_, v in mod_ms.items()}, "limiting_kernel":
+                    f"{limiting} (gemv_kernel{', fused TP exchange' if world > 1 and limiting in ('o', 'down') else ''})",
+                    "limiting_share_of_module_sum": mod_ms[limiting] / sum(mod_ms.values())}
     gu_bytes = sum(linear_bytes(lay[nm][3], lay[nm][4], K, M) for nm in ("gate", "up"))
-    gu_ms_med = statistics.median(gu_ms)
+    # the roofline kernel is gate_up's; a run without it (--modules) reports its first module's call
+    rl_mod = "gate_up" if "gate_up" in mod_ms else MODULES[0][0]
+    gu_ms_med = mod_ms[rl_mod]
+    if rl_mod != "gate_up":
+        gu_bytes = sum(linear_bytes(lay[nm][3], lay[nm][4], K, M) for nm in dict(MODULES)[rl_mod])
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -874,7 +894,7 @@ def main():
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = gu_bytes / (gu_ms_med * 1e-3) / 1e9
-    traffic = GEMV_TRAFFIC["bytes"] if (K == 4 and M == 1 and world == 1 and
+    traffic = GEMV_TRAFFIC["bytes"] if (K == 4 and M == 1 and world == 1 and rl_mod == "gate_up" and
                                          gemv_source_sha() == GEMV_TRAFFIC["src_sha256"]) else None
 
     # ---- end to end: pinned host x -> device, the layer's ops (graph), y -> pinned host ----
@@ -899,7 +919,7 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
-    del graphs, gu_graphs
+    del graphs, mod_graphs
 
     extra = {}
     if world == 1 and not args.no_extra:
@@ -968,7 +988,7 @@ def main():
         "step_ms_median": statistics.median(step_ms),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
-                     "kernel": "gate_up linear_groups call (gemv_kernel, graph-replayed), median "
+                     "kernel": f"{rl_mod} call (gemv_kernel, graph-replayed), median "
                                f"of {n_calls} event-timed calls, {gu_bytes} algorithmic bytes per call",
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemv_kernel "
                                        "launch of this call, captured from the current GEMV source" if traffic
@@ -978,6 +998,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 2),
                 "d2h_bytes_per_step": int(y_host.numel() * 2)},
         "gpu_launches": args.steps * len(MODULES),
+        "modules": modules_line,
         "clocks": clocks,
         **extra,
     }
