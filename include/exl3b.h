@@ -356,6 +356,14 @@ EXL3B_API int exl3b_rope_neox(uint16_t* qkv, int64_t ld, uint16_t* q_out, int64_
 EXL3B_API int exl3b_silu_mul(const uint16_t* in, int64_t ld_in, uint16_t* out, int64_t ld_out, int rows, int n,
                              void* stream);
 
+/* The fp8 input embedding (reference vllm_plugin/exl3rocm/ops.py:183-202, exl3rocm::fp8_embedding):
+ * out[t][0..dim) = fp16(table[ids[t]][0..dim)) for a float8_e4m3fn table [rows][dim] (no scale; the
+ * checkpoint's table cast as is).  ids int32 (ids_64 = 0) or int64 [n]; an id outside [0, rows) gives a
+ * zero row (vLLM masks ids outside a rank's vocab shard before the lookup).  dim % 16 == 0, table and
+ * out 16-byte aligned. */
+EXL3B_API int exl3b_fp8_embedding(const uint8_t* table, int64_t rows, int64_t dim, const void* ids, int ids_64,
+                                  int64_t n, uint16_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

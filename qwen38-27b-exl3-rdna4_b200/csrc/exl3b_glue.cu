@@ -10,6 +10,8 @@
 // kernel's results before its first read.
 #include <algorithm>
 
+#include <cuda_fp8.h>
+
 #include "exl3b_common.cuh"
 
 namespace exl3b {
@@ -156,6 +158,36 @@ static int glue_sms() {
     return v > 0 ? v : 148;
 }
 
+// ---------------------------------------------------------------------------------------------
+// fp8 (e4m3) input embedding: out[t][:] = fp16(table[ids[t]][:]).  One warp per token, 16 bytes
+// of the row per lane and step; every e4m3 value is exact in fp16 (the cast of torch's
+// .to(float16)).  An id outside [0, rows) writes a zero row.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) fp8_embedding_kernel(const uint8_t* table, int64_t rows, int64_t dim,
+                                                           const void* ids, int ids_64, int64_t n, __half* out) {
+    const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= n) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t id = ids_64 ? static_cast<const int64_t*>(ids)[t] : (int64_t)static_cast<const int32_t*>(ids)[t];
+    const bool ok = id >= 0 && id < rows;
+    const uint4* src = reinterpret_cast<const uint4*>(table + (ok ? id : 0) * dim);
+    uint4* dst = reinterpret_cast<uint4*>(out + t * dim);
+    for (int64_t c = lane; c < dim / 16; c += 32) {
+        const uint4 v = ok ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t h[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xFFFFu), __NV_E4M3);
+            const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
+            h[2 * i] = (uint32_t)lo.x | ((uint32_t)lo.y << 16);
+            h[2 * i + 1] = (uint32_t)hi.x | ((uint32_t)hi.y << 16);
+        }
+        dst[2 * c] = make_uint4(h[0], h[1], h[2], h[3]);
+        dst[2 * c + 1] = make_uint4(h[4], h[5], h[6], h[7]);
+    }
+}
+
 }  // namespace exl3b
 
 using namespace exl3b;
@@ -200,4 +232,16 @@ extern "C" int exl3b_silu_mul(const uint16_t* in, int64_t ld_in, uint16_t* out, 
     return cuda_status(launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), (cudaStream_t)stream,
                                   reinterpret_cast<const __half*>(in), ld_in, reinterpret_cast<__half*>(out), ld_out,
                                   rows, n));
+}
+
+extern "C" int exl3b_fp8_embedding(const uint8_t* table, int64_t rows, int64_t dim, const void* ids, int ids_64,
+                                   int64_t n, uint16_t* out, void* stream) {
+    if (rows <= 0 || dim <= 0 || n < 0) return EXL3B_BAD_ARG;
+    if (dim % 16) return EXL3B_DECLINED;
+    if (n == 0) return EXL3B_OK;
+    if (!table || !ids || !out || !aligned(table, 16) || !aligned(out, 16)) return EXL3B_BAD_ARG;
+    const unsigned grid = (unsigned)((n + 7) / 8);
+    fp8_embedding_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(table, rows, dim, ids, ids_64 ? 1 : 0, n,
+                                                                 reinterpret_cast<__half*>(out));
+    return cuda_status(cudaGetLastError());
 }

@@ -333,3 +333,29 @@ def exl3_linear_add_(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, 
         linear_into(x2, [trellis], [suh], [svh], K, mcg, mul1, r2, Y_ADD)
     else:
         r2.add_(exl3_linear(x2, trellis, suh, svh, K, mcg, mul1))
+
+
+# ---------------------------------------------------------------------------------------------
+# fp8 input embedding (reference vllm_plugin/exl3rocm/ops.py:183-202)
+# ---------------------------------------------------------------------------------------------
+@torch.library.custom_op("exl3rocm::fp8_embedding", mutates_args=())
+def fp8_embedding(weight: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    """Rows of a float8_e4m3fn table [vocab, hidden] gathered and cast to fp16 (the checkpoint's
+    table has no scale), shape [*ids.shape, hidden], by exl3b_fp8_embedding.  An opaque op, as in the
+    reference: a compiler tracing the gather would otherwise materialise a cast copy of the table."""
+    if weight.dtype != torch.float8_e4m3fn or weight.dim() != 2 or not weight.is_contiguous():
+        raise ValueError(f"exl3rocm::fp8_embedding: contiguous 2-d float8_e4m3fn table, not {weight.dtype} "
+                         f"{tuple(weight.shape)}")
+    flat = ids.reshape(-1)
+    if flat.dtype not in (torch.int32, torch.int64):
+        flat = flat.to(torch.int64)
+    flat = flat.contiguous()
+    out = torch.empty((flat.numel(), weight.shape[1]), dtype=torch.float16, device=weight.device)
+    _lib.call("exl3b_fp8_embedding", weight.data_ptr(), weight.shape[0], weight.shape[1], flat.data_ptr(),
+              1 if flat.dtype == torch.int64 else 0, flat.numel(), out.data_ptr(), _stream(weight.device))
+    return out.view(*ids.shape, weight.shape[1])
+
+
+@fp8_embedding.register_fake
+def _(weight, ids):
+    return weight.new_empty((*ids.shape, weight.shape[1]), dtype=torch.float16)

@@ -32,8 +32,9 @@ from torch.nn import Parameter
 
 from vllm.model_executor.layers.linear import LinearBase, LinearMethodBase, UnquantizedLinearMethod
 from vllm.model_executor.layers.quantization import register_quantization_config
-from vllm.model_executor.layers.quantization.base_config import QuantizationConfig
-from vllm.model_executor.layers.vocab_parallel_embedding import ParallelLMHead
+from vllm.model_executor.layers.quantization.base_config import QuantizationConfig, QuantizeMethodBase
+from vllm.model_executor.layers.vocab_parallel_embedding import ParallelLMHead, VocabParallelEmbedding
+from vllm.model_executor.utils import set_weight_attrs
 
 from . import sharding
 
@@ -76,6 +77,22 @@ def read_checkpoint_layout(model_dir: str) -> dict[str, tuple[int, int, int]]:
     return layout
 
 
+def read_checkpoint_embedding(model_dir: str) -> Optional[tuple[int, int]]:
+    """(vocab, hidden) of the language model's input embedding when the checkpoint stores it as
+    float8_e4m3fn (safetensors dtype ``F8_E4M3``), else None.  A vision tower's embedding does not
+    count, and neither do several candidates (reference plugin.py:117-120)."""
+    found = []
+    for path in sorted(glob.glob(os.path.join(model_dir, "*.safetensors"))):
+        with open(path, "rb") as f:
+            (hlen,) = struct.unpack("<Q", f.read(8))
+            header = json.loads(f.read(hlen))
+        for name, meta in header.items():
+            if (name != "__metadata__" and name.endswith("embed_tokens.weight") and meta.get("dtype") == "F8_E4M3"
+                    and "visual" not in name.split(".")):
+                found.append(tuple(meta["shape"]))
+    return found[0] if len(found) == 1 else None
+
+
 def _tp() -> tuple[int, int]:
     try:
         from vllm.distributed import get_tensor_model_parallel_rank, get_tensor_model_parallel_world_size
@@ -101,6 +118,11 @@ class Exl3Config(QuantizationConfig):
         super().__init__()
         self.codebook = codebook
         self.modules: dict[str, tuple[int, int, int]] = {}
+        self.embed_shape: Optional[tuple[int, int]] = None  # (vocab, hidden) of an fp8 input embedding
+
+    @property
+    def fp8_embedding(self) -> bool:
+        return self.embed_shape is not None
 
     def __repr__(self):
         widths = sorted({K for K, _, _ in self.modules.values()})
@@ -130,6 +152,7 @@ class Exl3Config(QuantizationConfig):
             raise NotImplementedError(f"exl3: {model_name!r} is not a directory; the EXL3 module map is read "
                                       "from the checkpoint's safetensors headers")
         self.modules = read_checkpoint_layout(model_name)
+        self.embed_shape = read_checkpoint_embedding(model_name)
 
     def groups_for(self, prefix: str) -> Optional[list[tuple[str, int, int, int]]]:
         """[(member, K, k, n)] for the checkpoint tensors behind the (possibly fused) vLLM module at
@@ -149,12 +172,143 @@ class Exl3Config(QuantizationConfig):
     def get_quant_method(self, layer: torch.nn.Module, prefix: str):
         is_linear = isinstance(layer, LinearBase)
         if not (is_linear or isinstance(layer, ParallelLMHead)):
+            # the input embedding stays in the checkpoint's fp8 (reference plugin.py:158-159)
+            if (isinstance(layer, VocabParallelEmbedding) and self.fp8_embedding
+                    and prefix.endswith("embed_tokens")):
+                return Fp8EmbeddingMethod()
             return None
         groups = self.groups_for(prefix)
         if groups is not None:
             return Exl3LinearMethod(self, groups)
         # a plain (unquantised) linear keeps vLLM's method; an lm_head keeps vLLM's default
         return UnquantizedLinearMethod() if is_linear else None
+
+
+class Fp8EmbeddingMethod(QuantizeMethodBase):
+    """The input embedding kept as the checkpoint's float8_e4m3fn table (no scale) and looked up with
+    ``exl3rocm::fp8_embedding``: half the memory of an fp16 table (reference plugin.py:215-233).  Under
+    tensor parallelism vLLM hands each rank its vocab rows (``output_partition_sizes``) and masks the
+    ids outside them."""
+
+    def create_weights(self, layer, input_size_per_partition, output_partition_sizes, input_size, output_size,
+                       params_dtype, **extra_weight_attrs):
+        weight = Parameter(torch.empty(sum(output_partition_sizes), input_size_per_partition,
+                                       dtype=torch.float8_e4m3fn), requires_grad=False)
+        set_weight_attrs(weight, {"input_dim": 1, "output_dim": 0})
+        set_weight_attrs(weight, extra_weight_attrs)
+        layer.register_parameter("weight", weight)
+
+    def apply(self, layer, x, bias=None):
+        raise NotImplementedError("exl3: the fp8 input embedding is not an output head")
+
+    def embedding(self, layer, input_):
+        from . import ops  # noqa: F401  registers torch.ops.exl3rocm.fp8_embedding
+        return torch.ops.exl3rocm.fp8_embedding(layer.weight, input_)
+
+
+def wants_fp8_embedding(quant_config, num_embeddings: int, embedding_dim: int) -> bool:
+    """True for a plain input embedding built without a quant config, of exactly the shape of the
+    checkpoint's fp8 table, while an exl3 model with such a table is being built."""
+    return (isinstance(quant_config, Exl3Config) and quant_config.fp8_embedding
+            and (num_embeddings, embedding_dim) == tuple(quant_config.embed_shape))
+
+
+def _install_fp8_embedding_hook() -> bool:
+    """Models build their input embedding as ``VocabParallelEmbedding(vocab, hidden)`` without the
+    quant config, so no quantisation method could keep the fp8 table and vLLM would load it as fp16
+    (reference plugin.py:405-425).  While vLLM's current config is an exl3 one with an fp8 embedding,
+    a plain VocabParallelEmbedding of the table's shape gets that config (and the ``embed_tokens``
+    prefix), so that get_quant_method picks Fp8EmbeddingMethod.  Returns whether the hook went in."""
+    import inspect
+    try:
+        from vllm.config import get_current_vllm_config_or_none
+    except ImportError:
+        return False
+    if getattr(VocabParallelEmbedding, "_exl3_fp8_hook", False):
+        return False
+    orig = VocabParallelEmbedding.__init__
+    sig = inspect.signature(orig)
+
+    def __init__(self, *args, **kwargs):
+        if type(self) is VocabParallelEmbedding:
+            bound = sig.bind(self, *args, **kwargs)
+            a = bound.arguments
+            cfg = get_current_vllm_config_or_none()
+            qc = getattr(cfg, "quant_config", None) if cfg is not None else None
+            if a.get("quant_config") is None and wants_fp8_embedding(qc, a["num_embeddings"], a["embedding_dim"]):
+                a["quant_config"] = qc
+                a["prefix"] = a.get("prefix") or "embed_tokens"
+                return orig(*bound.args, **bound.kwargs)
+        return orig(self, *args, **kwargs)
+
+    VocabParallelEmbedding.__init__ = __init__
+    VocabParallelEmbedding._exl3_fp8_hook = True
+    return True
+
+
+def _speculative() -> bool:
+    try:
+        from vllm.config import get_current_vllm_config_or_none
+        cfg = get_current_vllm_config_or_none()
+    except ImportError:
+        return False
+    return cfg is not None and getattr(cfg, "speculative_config", None) is not None
+
+
+def prune_draft_head(layer) -> bool:
+    """The MTP drafter's pruned lm_head without a copy (reference plugin.py:431-486): the head's columns
+    are re-stored as three groups [drafted prefix | middle | drafted tail] (``sharding.draft_bounds``,
+    ``EXL3_DRAFT_VOCAB_BLOCKS`` prefix blocks, default 640, plus the last 16).  The target runs all three
+    in order, so its logits are unchanged; the drafter runs groups 0 and 2 only.  Applied to an
+    unsharded head (TP 1, as the reference); under tensor parallelism the drafter keeps the full head.
+    Returns whether the head was split."""
+    shard = layer.exl3_shard
+    if len(shard.shards) != 1 or shard.tp_size != 1 or shard.shards[0].trimmed:
+        return False
+    n = shard.shards[0].stored_n
+    bounds = sharding.draft_bounds(n, int(os.environ.get("EXL3_DRAFT_VOCAB_BLOCKS", "640")))
+    if bounds is None:
+        return False
+    a, b = bounds
+    shard.split_columns([a, b])
+    dev = shard.shards[0].trellis.device
+    layer.exl3_draft_groups = (0, 2)
+    layer.exl3_draft_cols = torch.cat([torch.arange(0, a, device=dev), torch.arange(b, n, device=dev)])
+    return True
+
+
+def draft_logits(lm_head, hidden_states: torch.Tensor) -> torch.Tensor:
+    """The drafter's logits over the pruned head: the drafted columns computed, -inf elsewhere."""
+    sub = lm_head.exl3_shard.forward_groups(hidden_states, lm_head.exl3_draft_groups, lm_head.exl3_mcg,
+                                            lm_head.exl3_mul1)
+    logits = sub.new_full((sub.shape[0], lm_head.exl3_shard.shards[-1].c1), float("-inf"))
+    logits.index_copy_(1, lm_head.exl3_draft_cols, sub)
+    return logits
+
+
+def _install_draft_logits_patch(cls=None) -> bool:
+    """Qwen3.5's MTP drafter computes its logits through the pruned head when the shared lm_head was
+    split (reference plugin.py:489-528); otherwise vLLM's own compute_logits runs."""
+    if cls is None:
+        try:
+            from vllm.model_executor.models import qwen3_5_mtp
+        except Exception:
+            return False
+        cls = getattr(qwen3_5_mtp, "Qwen3_5MTP", None)
+    if cls is None or getattr(cls, "_exl3_draft_patch", False):
+        return False
+    orig = cls.compute_logits
+
+    def compute_logits(self, hidden_states, spec_step_idx: int = 0):
+        lm = self.lm_head
+        if getattr(lm, "exl3_draft_groups", None) is None:
+            return orig(self, hidden_states, spec_step_idx)
+        logits = draft_logits(lm, hidden_states)
+        return logits[:, : self.config.vocab_size].to(hidden_states.dtype)
+
+    cls.compute_logits = compute_logits
+    cls._exl3_draft_patch = True
+    return True
 
 
 def parallel_mode(input_size_per_partition: int, input_size: int, output_partition_sizes: list[int],
@@ -204,10 +358,12 @@ class Exl3LinearMethod(LinearMethodBase):
     ``svh`` (and the codebook scalar) are 0-size load targets that vLLM's name mapping resolves to;
     their weight_loader slices each full checkpoint tensor into this rank's shard."""
 
-    def __init__(self, config: Exl3Config, groups, tp: Optional[tuple[int, int]] = None):
+    def __init__(self, config: Exl3Config, groups, tp: Optional[tuple[int, int]] = None,
+                 drafting: Optional[bool] = None):
         self.config = config
         self.groups = groups  # [(member, K, k, n)]
         self.tp = tp          # (size, rank); None = ask vLLM at create_weights
+        self.drafting = drafting  # a speculative (MTP) drafter shares this lm_head; None = ask vLLM
 
     def create_weights(self, layer, input_size_per_partition, output_partition_sizes, input_size, output_size,
                        params_dtype, **extra_weight_attrs):
@@ -226,6 +382,8 @@ class Exl3LinearMethod(LinearMethodBase):
         if self.config.codebook in CODEBOOK_SCALARS:  # only what the checkpoint stores is registered
             targets.append(self.config.codebook)
         layer.exl3_load_targets = tuple(targets)
+        if self.drafting is None:
+            self.drafting = isinstance(layer, ParallelLMHead) and _speculative()
         for kind in targets:
             target = Parameter(torch.empty(0, dtype=torch.int8), requires_grad=False)
             target.weight_loader = _ShardLoader(layer, kind)
@@ -243,6 +401,8 @@ class Exl3LinearMethod(LinearMethodBase):
         # the load targets have served their purpose; weights live in the shard
         for kind in layer.exl3_load_targets:
             layer._parameters.pop(kind, None)
+        if self.drafting and isinstance(layer, ParallelLMHead):
+            prune_draft_head(layer)
 
     def apply(self, layer, x, bias=None):
         y = layer.exl3_shard.forward(x, layer.exl3_mcg, layer.exl3_mul1)
@@ -426,6 +586,10 @@ def _install_kv_hooks():
 def register():
     """vllm.general_plugins entry point (runs in every vLLM process)."""
     from . import ops  # noqa: F401  registers torch.ops.exl3rocm.*
+    if os.environ.get("EXL3_FP8_EMBEDDING", "1") != "0":
+        _install_fp8_embedding_hook()
+    if os.environ.get("EXL3_DRAFT_VOCAB_BLOCKS", "640") != "0":
+        _install_draft_logits_patch()
     if os.environ.get("EXL3_KV_ROUTING", "1") != "0":
         _install_kv_hooks()
     return None

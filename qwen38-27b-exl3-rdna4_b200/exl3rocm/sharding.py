@@ -202,6 +202,44 @@ class ModuleShard:
         y = torch.ops.exl3rocm.linear_groups(self.local_x(x), tr, su, sv, Ks, mcg, mul1)
         return self.trim(y)
 
+    def forward_groups(self, x: torch.Tensor, groups: Sequence[int], mcg: bool, mul1: bool) -> torch.Tensor:
+        """The output columns of the listed groups only, concatenated in their order (untrimmed
+        shards: the draft head below)."""
+        tr, su, sv, Ks = self.tensors()
+        return torch.ops.exl3rocm.linear_groups(self.local_x(x), [tr[g] for g in groups], [su[g] for g in groups],
+                                                [sv[g] for g in groups], [Ks[g] for g in groups], mcg, mul1)
+
+    def split_columns(self, cuts: Sequence[int]) -> None:
+        """Re-store a loaded one-group, untrimmed shard as consecutive column groups cut at ``cuts``
+        (absolute output columns, multiples of 128 strictly inside the stored range), each with its
+        own contiguous trellis and svh and the shared suh.  The full output (all groups in order) is
+        unchanged; the parts replace the original tensors, so no copy outlives the call."""
+        if len(self.shards) != 1 or self.shards[0].trimmed or self.parallel == "row":
+            raise ValueError("exl3rocm: split_columns takes one untrimmed column group")
+        s, g = self.shards[0], self.groups[0]
+        bounds = [s.c0, *cuts, s.c1]
+        if any(b % BLOCK for b in cuts) or any(a >= b for a, b in zip(bounds, bounds[1:])):
+            raise ValueError(f"exl3rocm: cuts {list(cuts)} do not split columns [{s.c0}, {s.c1}) into 128-blocks")
+        parts = []
+        for a, b in zip(bounds, bounds[1:]):
+            tr = s.trellis[:, (a - s.c0) // TILE:(b - s.c0) // TILE, :].contiguous()
+            sv = s.svh[a - s.c0:b - s.c0].contiguous()
+            parts.append(GroupShard(s.K, s.k0, s.k1, a, b, 0, b - a, tr, s.suh, sv))
+        self.shards = parts
+        self.groups = [Group(f"{g.name}[{a}:{b}]", g.K, g.k, b - a) for a, b in zip(bounds, bounds[1:])]
+        self.loaded = {(k, i) for k in ("trellis", "suh", "svh") for i in range(len(parts))}
+
+
+def draft_bounds(n: int, draft_blocks: int, tail_blocks: int = 16) -> Optional[tuple[int, int]]:
+    """Columns an MTP drafter scores of an n-column lm_head: the first ``draft_blocks`` 128-column
+    blocks (BPE ids run roughly by frequency) and the last ``tail_blocks`` (special and chat tokens),
+    as (a, b) for the column ranges [0, a) and [b, n); None when that is the whole head (reference
+    plugin.py:431-441)."""
+    nb = n // BLOCK
+    if draft_blocks <= 0 or draft_blocks + tail_blocks >= nb:
+        return None
+    return draft_blocks * BLOCK, (nb - tail_blocks) * BLOCK
+
 
 def partition_owners(partitions: Sequence[int], widths: Sequence[int]) -> list[int]:
     """The group each of vLLM's output partitions falls in, given the groups' output widths on this rank.
