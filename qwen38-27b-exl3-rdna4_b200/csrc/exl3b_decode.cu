@@ -48,33 +48,71 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint16_t* __restrict
     *reinterpret_cast<uint4*>(dst) = v;
 }
 
-// One warp per (row, 128-column block).
-__global__ void had128_kernel(const __half* in, int64_t ld_in, __half* out, int64_t ld_out, int64_t rows,
-                              int64_t blocks, const __half* __restrict__ pre, const __half* __restrict__ post,
-                              float scale) {
-    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (item >= rows * blocks) return;
-    const int lane = threadIdx.x & 31;
-    const int64_t r = item / blocks, b = item % blocks;
-    const int64_t c = b * 128 + 4 * lane;
-    const uint2 raw = *reinterpret_cast<const uint2*>(in + r * ld_in + c);
-    __half2 h01 = u32_as_h2(raw.x), h23 = u32_as_h2(raw.y);
-    if (pre) {
-        const uint2 p = *reinterpret_cast<const uint2*>(pre + c);
-        h01 = __hmul2(h01, u32_as_h2(p.x));
-        h23 = __hmul2(h23, u32_as_h2(p.y));
+// Four lanes per (row, 128-column block), eight blocks per warp.  Lane j of a block holds its
+// 4-element chunks l = j + 4i (i = 0..7): H4 inside a chunk, then chunk distances 1 and 2 between the
+// block's lanes and 4, 8, 16 inside a lane, the operations and order of had128_warp (a warp holding
+// chunk l in lane l), so the results are the same bit for bit with two shuffle stages instead of five
+// (one warp per block ran 77 us for 213 MB, issue-bound on its shuffles).
+constexpr int kHadBlocksPerWarp = 8;
+__global__ void __launch_bounds__(256) had128_kernel(const __half* in, int64_t ld_in, __half* out, int64_t ld_out,
+                                                     int64_t rows, int64_t blocks, const __half* __restrict__ pre,
+                                                     const __half* __restrict__ post, float scale) {
+    const int lane = threadIdx.x & 31, j = lane & 3;
+    const int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kHadBlocksPerWarp +
+                         (lane >> 2);
+    const bool live = item < rows * blocks;  // dead lanes run along (they take part in the shuffles)
+    const int64_t r = live ? item / blocks : 0, b = live ? item % blocks : 0;
+    float v[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t c = b * 128 + 16 * i + 4 * j;
+        uint2 raw = live ? *reinterpret_cast<const uint2*>(in + r * ld_in + c) : make_uint2(0u, 0u);
+        __half2 h01 = u32_as_h2(raw.x), h23 = u32_as_h2(raw.y);
+        if (pre && live) {
+            const uint2 p = *reinterpret_cast<const uint2*>(pre + c);
+            h01 = __hmul2(h01, u32_as_h2(p.x));
+            h23 = __hmul2(h23, u32_as_h2(p.y));
+        }
+        const float x0 = __low2float(h01), x1 = __high2float(h01), x2 = __low2float(h23), x3 = __high2float(h23);
+        const float s0 = x0 + x1, d0 = x0 - x1, s1 = x2 + x3, d1 = x2 - x3;
+        v[i][0] = s0 + s1; v[i][1] = d0 + d1; v[i][2] = s0 - s1; v[i][3] = d0 - d1;
     }
-    float v[4] = {__low2float(h01), __high2float(h01), __low2float(h23), __high2float(h23)};
-    had128_warp(v);
+#pragma unroll
+    for (int d = 1; d <= 2; d <<= 1) {
+        const bool upper = (j & d) != 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float o = __shfl_xor_sync(0xFFFFFFFFu, v[i][e], d);
+                v[i][e] = upper ? (o - v[i][e]) : (v[i][e] + o);
+            }
+    }
+#pragma unroll
+    for (int d = 1; d <= 4; d <<= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (!(i & d))
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float lo = v[i][e], hi = v[i | d][e];
+                    v[i][e] = lo + hi;
+                    v[i | d][e] = lo - hi;
+                }
+    if (!live) return;
     const float s = kRScale * scale;
-    h01 = __floats2half2_rn(v[0] * s, v[1] * s);
-    h23 = __floats2half2_rn(v[2] * s, v[3] * s);
-    if (post) {
-        const uint2 q = *reinterpret_cast<const uint2*>(post + c);
-        h01 = __hmul2(h01, u32_as_h2(q.x));
-        h23 = __hmul2(h23, u32_as_h2(q.y));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t c = b * 128 + 16 * i + 4 * j;
+        __half2 h01 = __floats2half2_rn(v[i][0] * s, v[i][1] * s);
+        __half2 h23 = __floats2half2_rn(v[i][2] * s, v[i][3] * s);
+        if (post) {
+            const uint2 q = *reinterpret_cast<const uint2*>(post + c);
+            h01 = __hmul2(h01, u32_as_h2(q.x));
+            h23 = __hmul2(h23, u32_as_h2(q.y));
+        }
+        *reinterpret_cast<uint2*>(out + r * ld_out + c) = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
     }
-    *reinterpret_cast<uint2*>(out + r * ld_out + c) = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
 }
 
 template <int CB>
@@ -138,7 +176,8 @@ extern "C" int exl3b_had128(const uint16_t* in, int64_t ld_in, uint16_t* out, in
     if (!aligned(in, 8) || !aligned(out, 8) || (pre && !aligned(pre, 8)) || (post && !aligned(post, 8)))
         return EXL3B_BAD_ARG;
     const int64_t items = rows * (cols / 128);
-    const unsigned grid = (unsigned)((items + 7) / 8);
+    const int64_t per_block = 8 * kHadBlocksPerWarp;  // 8 warps per CTA
+    const unsigned grid = (unsigned)((items + per_block - 1) / per_block);
     had128_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<const __half*>(in), ld_in, reinterpret_cast<__half*>(out), ld_out, rows, cols / 128,
         reinterpret_cast<const __half*>(pre), reinterpret_cast<const __half*>(post), scale);
