@@ -470,19 +470,23 @@ SWEEP_SHAPES = [("q/o", HIDDEN, HIDDEN), ("k/v", HIDDEN, KV_HEADS * HEAD_DIM), (
 
 def bench_sweep(torch, dev, rows=(1, 4, 8, 16, 128, 2048), bits=(2, 3, 4, 5, 6, 8), iters: int = 10) -> list:
     """The M / bit-width sweep on the layer shapes, through the public op, L2 flushed between calls:
-    every M at 4 bits on every shape, and every bit width at M = 1 and M = 2048 on gate/up.
-    M <= 16 reports GB/s of algorithmic bytes (HBM-bound GEMV), M >= 128 TFLOP/s (tensor-bound GEMM)."""
+    every M at 4 bits on every shape, and every bit width at M = 1 and M = 2048 on gate/up, all in the
+    mul1 codebook (the reference's production one), plus a spot check of 3INST (cb0)
+    at M = 1 and 2048 on gate/up.  M <= 16 reports GB/s of algorithmic bytes (HBM-bound GEMV), M >= 128
+    TFLOP/s (tensor-bound GEMM)."""
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
-    points = [(nm, k, n, m, 4) for nm, k, n in SWEEP_SHAPES for m in rows]
-    points += [("gate/up", HIDDEN, INTER, m, K) for K in bits if K != 4 for m in (1, 2048)]
+    points = [(nm, k, n, m, 4, "mul1") for nm, k, n in SWEEP_SHAPES for m in rows]
+    points += [("gate/up", HIDDEN, INTER, m, K, "mul1") for K in bits if K != 4 for m in (1, 2048)]
+    points += [("gate/up", HIDDEN, INTER, m, 4, "3inst") for m in (1, 2048)]
     out = []
-    for nm, k, n, m, K in points:
+    for nm, k, n, m, K, cb in points:
         g, tr, suh, svh = _layer_weights(torch, dev, k, n, K, 7 + k + n + K)
         x = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
-        op = lambda: torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, True)
+        mul1 = cb == "mul1"
+        op = lambda: torch.ops.exl3rocm.linear(x, tr, suh, svh, K, False, mul1)
         op()
         ms = _event_ms(torch, op, iters, flush)
-        rec = {"shape": nm, "k": k, "n": n, "m": m, "bits": K, "ms": ms}
+        rec = {"shape": nm, "k": k, "n": n, "m": m, "bits": K, "codebook": cb, "ms": ms}
         if m <= 16:
             rec["gb_s"] = linear_bytes(k, n, K, m) / (ms * 1e-3) / 1e9
         else:
