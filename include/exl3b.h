@@ -92,6 +92,12 @@ EXL3B_API int exl3b_had128(const uint16_t* in, int64_t ld_in, uint16_t* out, int
 #define EXL3B_WS_ZERO_BYTES (256 + 4 * 8192)
 EXL3B_API size_t exl3b_linear_workspace_bytes(int m, int k, int groups, int64_t n_total);
 
+/* 1 when exl3b_linear takes an m x k x n call at K bits in this codebook (EXL3B_X_BF16 / EXL3B_Y_ADD may be
+ * or-ed in), else 0: m <= EXL3B_GEMV_MAX_ROWS, k and n multiples of 128, 1 <= K <= 8.  Host-only, no device
+ * needed.  Replaces exllamav3_ext.exl3_gemv_mr_supported(m, k, n, K, mcg, mul1) (reference
+ * vllm_plugin/exl3rocm/ops.py:83,149; 0002-gemv-multirow.patch:334-338). */
+EXL3B_API int exl3b_linear_supported(int m, int k, int n, int K, int codebook);
+
 /* The EXL3 linear for 1 <= m <= 16 (decode / speculative verify):
  *   y[m][n] = had_out( fp16( had_in(x, suh) @ W ), svh )
  * x fp16 [m][k] contiguous, trellis int16 [k/16][n/16][16K], suh fp16 [k], svh fp16 [n],

@@ -1077,6 +1077,14 @@ extern "C" size_t exl3b_linear_workspace_bytes(int m, int k, int groups, int64_t
     return ws_layout(m, k, groups, q, groups == 2 ? n_total : 0).total;
 }
 
+extern "C" int exl3b_linear_supported(int m, int k, int n, int K, int codebook) {
+    // the shape rules of linear_impl for one group, without touching a device
+    const int flags = EXL3B_X_BF16 | EXL3B_Y_ADD;  // the flags that do not change the shape rules
+    codebook &= ~flags;
+    return (m >= 1 && m <= EXL3B_GEMV_MAX_ROWS && k > 0 && k % 128 == 0 && n > 0 && n % 128 == 0 &&
+            n / 128 <= kMaxBlocks && K >= 1 && K <= 8 && codebook >= 0 && codebook <= 2) ? 1 : 0;
+}
+
 extern "C" int exl3b_linear(const uint16_t* x, int m, int k, const uint16_t* trellis, int n, int K, int codebook,
                             const uint16_t* suh, const uint16_t* svh, uint16_t* y, int64_t ldy, void* workspace,
                             size_t workspace_bytes, void* stream) {

@@ -56,6 +56,7 @@ SIGNATURES = {
     "exl3b_gemm_workspace_bytes": (sz, [i32, i32]),
     "exl3b_gemm": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp, sz, c_vp]),
     "exl3b_decode_ceiling": (i32, [i32, i32, c_vp, i32, c_vp, c_vp, c_vp]),
+    "exl3b_linear_supported": (i32, [i32, i32, i32, i32, i32]),
     "exl3b_fp8_embedding": (i32, [c_vp, i64, i64, c_vp, i32, i64, c_vp, c_vp]),
     "exl3b_linear_noalloc": (i32, [c_vp, i32, i32, c_vp, i32, i32, i32, c_vp, c_vp, c_vp, i64, c_vp]),
     "exl3b_linear_noalloc_error": (i32, [ctypes.POINTER(i32), c_vp]),

@@ -209,6 +209,12 @@ def _linear_large(x2: torch.Tensor, trellis: torch.Tensor, suh, svh, K: int, mcg
 # ---------------------------------------------------------------------------------------------
 # the custom ops (reference ops.py:65-180)
 # ---------------------------------------------------------------------------------------------
+def linear_supported(m: int, k: int, n: int, K: int, mcg: bool, mul1: bool) -> bool:
+    """Whether the decode GEMV takes an m x k x n call (exl3b_linear_supported; the reference asks
+    exl3_gemv_mr_supported the same, ops.py:83)."""
+    return bool(_lib.lib().exl3b_linear_supported(m, k, n, K, _cb(mcg, mul1)))
+
+
 @torch.library.custom_op("exl3rocm::linear", mutates_args=())
 def exl3_linear(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor,
                 K: int, mcg: bool, mul1: bool) -> torch.Tensor:

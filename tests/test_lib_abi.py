@@ -65,6 +65,28 @@ def test_linear_declines_before_launch(m, k, n, K, cb, expect):
     assert st == expect
 
 
+@pytest.mark.parametrize("m,k,n,K,cb", [
+    (17, 256, 128, 4, 2), (0, 256, 128, 4, 2), (1, 200, 128, 4, 2), (1, 256, 100, 4, 2),
+    (1, 256, 128, 9, 2), (1, 256, 128, 0, 2), (1, 256, 128, 4, 3), (1, 256, 128 * 8193, 4, 2),
+])
+def test_supported_query_agrees_with_declines(m, k, n, K, cb):
+    L = _lib.lib()
+    assert L.exl3b_linear_supported(m, k, n, K, cb) == 0
+    assert L.exl3b_linear(FAKE, m, k, FAKE, n, K, cb, FAKE, FAKE, FAKE, n, FAKE, 1 << 30, None) == \
+        _lib.EXL3B_DECLINED
+
+
+def test_supported_query_takes_decode_shapes():
+    from exl3rocm import ops
+    L = _lib.lib()
+    for m in (1, 4, 16):
+        for K in range(1, 9):
+            for cb in (0, 1, 2, 2 | ops.X_BF16, 2 | ops.Y_ADD):
+                assert L.exl3b_linear_supported(m, 5120, 34816, K, cb) == 1
+    assert ops.linear_supported(1, 5120, 5120, 4, False, True)
+    assert not ops.linear_supported(32, 5120, 5120, 4, False, True)
+
+
 def test_linear_rejects_small_workspace_and_nulls():
     L = _lib.lib()
     assert L.exl3b_linear(FAKE, 1, 256, FAKE, 128, 4, 2, FAKE, FAKE, FAKE, 128, FAKE, 16, None) == \
