@@ -72,6 +72,7 @@ struct GemvParams {
     float* partials;      // workspace: [ctas + super-blocks - 1][m][sb_cols], slot = cta + super-block
     int* counters;        // workspace: one per global column block
     int* err;             // workspace error word
+    unsigned long long* ticket;  // workspace: the slot ticket counter (never reset)
     int groups, m, k, kt;  // kt = k / 16
     int ku;               // units per super-block = kt / (R0 * q)
     int q;                // k-rows per 64-tile stage slot (super-blocks of 64 / q n-tiles): 1, 2 or 4
@@ -118,8 +119,15 @@ EXL3B_DEV uint4 ld_pairs(const uint32_t* p) {
 // ---------------------------------------------------------------------------------------------
 // stream-K partition helpers (64-bit: U * P fits easily)
 // ---------------------------------------------------------------------------------------------
-EXL3B_DEV int unit_start(int c, int U, int P) { return (int)(((int64_t)c * U) / P); }
-EXL3B_DEV int cta_of_unit(int u, int U, int P) { return (int)((((int64_t)u + 1) * P - 1) / U); }
+// Slot c of P (U >= P units) takes units [unit_start(c), unit_start(c + 1)): the first U % P slots
+// one unit more than the rest.  Slots are handed out in the order the CTAs start (see the kernel), so
+// the CTAs that start last -- on the SMs the previous kernel's finishing CTAs leave last -- take the
+// lighter shares.
+EXL3B_DEV int unit_start(int c, int U, int P) { return c * (U / P) + min(c, U % P); }
+EXL3B_DEV int cta_of_unit(int u, int U, int P) {
+    const int b = U / P, e = U % P, heavy = e * (b + 1);
+    return u < heavy ? u / (b + 1) : e + (u - heavy) / b;
+}
 
 struct SbInfo {
     int g;     // group
@@ -159,7 +167,7 @@ struct GemvSmem {
 
 // Runtime part of the layout (depends on m): ring, accumulator tile, then full[S], empty[S]
 // barriers; flags: abort (int), the flush's abort snapshot (int), the finish decision of each column
-// block shared by its two warps (8 ints); then the fused RMSNorm's 1/rms of each row.
+// block shared by its two warps (8 ints), the CTA's stream-K slot (int); then the fused RMSNorm's 1/rms of each row.
 struct GemvLayout {
     int stages, acc_off, bar_off, flag_off, norm_off, total;
 };
@@ -418,11 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     // the producer has read them (the first flush follows the first published unit)
     float* norm_part = reinterpret_cast<float*>(smem + lay.acc_off);
 
-    const int c = blockIdx.x, P = p.ctas, U = p.units, ku = p.ku, m = p.m;
-    const int u0 = unit_start(c, U, P), u1 = unit_start(c + 1, U, P);
-    const int nunits = u1 - u0;
-
+    volatile int* slot_s = abort_flag + 10;  // this CTA's stream-K slot
     if (threadIdx.x == 0) {
+        // Slots in start order: P consecutive tickets of the ever-growing 64-bit counter are P
+        // distinct slots mod P.  Every CTA takes its ticket before griddepcontrol.launch_dependents,
+        // so no later launch's tickets interleave with this one's.  The slot decides the work, never
+        // the arithmetic: a slot's partial sums are the same whichever CTA runs it.
+        const unsigned long long t = atomicAdd(p.ticket, 1ull);
+        *slot_s = (int)(t % (unsigned long long)p.ctas);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, kDecodeWarps);
@@ -431,6 +442,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         fence_mbar_init();
     }
     __syncthreads();
+    const int c = *slot_s, P = p.ctas, U = p.units, ku = p.ku, m = p.m;
+    const int u0 = unit_start(c, U, P), u1 = unit_start(c + 1, U, P);
+    const int nunits = u1 - u0;
 
     griddep_launch();  // the next kernel in the stream may start its own prologue
 
@@ -816,7 +830,8 @@ static cudaError_t launch_ceiling_k(int K, const uint16_t* trellis, int iters, f
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-constexpr size_t kHeaderBytes = 256;
+constexpr size_t kHeaderBytes = 256;  // error word at 0, slot ticket counter at kTicketOffset
+constexpr size_t kTicketOffset = 128;
 // Counter region of fixed size (one int per global 128-column block, up to kMaxBlocks), so that
 // calls of any shape find their counters at the same zeroed place.
 constexpr int kMaxBlocks = 8192;
@@ -1027,6 +1042,7 @@ int linear_impl(const uint16_t* x, int m, int k, int groups, const uint16_t* con
     p.partials = reinterpret_cast<float*>(ws + L.partials);
     p.counters = reinterpret_cast<int*>(ws + L.counters);
     p.err = reinterpret_cast<int*>(ws);
+    p.ticket = reinterpret_cast<unsigned long long*>(ws + kTicketOffset);
     p.groups = groups;
     p.m = m;
     p.k = k;
