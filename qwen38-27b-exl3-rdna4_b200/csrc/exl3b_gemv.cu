@@ -165,11 +165,11 @@ struct GemvSmem {
     static_assert((kBudget - 8 * MT * kAccCols * 4 - kTail) / kStageBytes >= 2, "shared-memory ring too small");
 };
 
-// Runtime part of the layout (depends on m): ring, accumulator tile, then full[S], empty[S]
+// Runtime part of the layout (depends on m): ring, accumulator tile, the m == 1 run sums, full[S], empty[S]
 // barriers; flags: abort (int), the flush's abort snapshot (int), the finish decision of each column
 // block shared by its two warps (8 ints), the CTA's stream-K slot (int); then the fused RMSNorm's 1/rms of each row.
 struct GemvLayout {
-    int stages, acc_off, bar_off, flag_off, norm_off, total;
+    int stages, acc_off, hi_off, bar_off, flag_off, norm_off, total;
 };
 template <int K, int MT, int R0>
 __host__ __device__ inline GemvLayout gemv_layout(int m) {
@@ -179,7 +179,10 @@ __host__ __device__ inline GemvLayout gemv_layout(int m) {
     L.stages = (S::kBudget - 8 * MT * kAccCols * 4 - S::kTail) / S::kStageBytes;
     if (L.stages > S::kMaxStages) L.stages = S::kMaxStages;
     L.acc_off = L.stages * S::kStageBytes;
-    L.bar_off = L.acc_off + acc;
+    // m == 1: the second run sums of the flush, 128 floats per column block, inside the room the
+    // budget keeps for 8 MT accumulator rows
+    L.hi_off = L.acc_off + acc;
+    L.bar_off = L.hi_off + (m == 1 ? 8 * 128 * 4 : 0);
     L.flag_off = L.bar_off + 2 * L.stages * 8;
     L.norm_off = L.flag_off + 64;
     L.total = L.norm_off + 4 * EXL3B_GEMV_MAX_ROWS;
@@ -187,20 +190,20 @@ __host__ __device__ inline GemvLayout gemv_layout(int m) {
 }
 
 // Decode warps blk (half 0) and blk + 8 (half 1) finish column block `blk` of super-block `sb`
-// (only when a CTA leaves a super-block); with m > 1 each takes half of the rows, half 0 the first
-// ceil(m / 2), so twice the partial loads are in flight.  With m == 1 warp blk works alone.  The two
-// warps meet at named barrier kPairBar0 + blk; `fin` is their shared decision word.
+// (only when a CTA leaves a super-block); each takes half of the rows, half 0 the first ceil(m / 2).
+// The partials of the CTAs that shared the block are summed as two runs, CTAs cf..mid-1 and mid..cl,
+// each in CTA order, then added: with m == 1 half 1 sums the second run of row 0 (into hi_s) while
+// half 0 sums the first, so two warps' loads are in flight; with m > 1 each warp sums both runs of its
+// rows itself.  Every row takes the same operations either way, so it is bitwise the same for every m.
+// The two warps meet at named barrier kPairBar0 + blk; `fin` is their shared decision word.
 template <int MT>
-__device__ __forceinline__ void flush_block(const GemvParams& p, const float* acc_s, volatile int* abort_flag, int c,
-                                         int sb, SbInfo si, int blk, int half, int u0, int u1, int lane,
-                                         volatile int* fin) {
+__device__ __forceinline__ void flush_block(const GemvParams& p, const float* acc_s, float* hi_s,
+                                         volatile int* abort_flag, int c, int sb, SbInfo si, int blk, int half,
+                                         int u0, int u1, int lane, volatile int* fin) {
     const int ku = p.ku, U = p.units, P = p.ctas, m = p.m;
-    const bool pair = m > 1;
     const int mh = (m + 1) >> 1;
-    const int r_lo = pair ? half * mh : 0, r_hi = pair ? (half ? m : mh) : m;  // this warp's rows
-    auto pair_sync = [&]() {
-        if (pair) named_bar(kPairBar0 + blk, 64);
-    };
+    const int r_lo = half * mh, r_hi = half ? m : mh;  // this warp's rows (none for half 1 when m == 1)
+    auto pair_sync = [&]() { named_bar(kPairBar0 + blk, 64); };
     // If this CTA covered the super-block's whole k range, transform and store; otherwise
     // publish the partial and, if it is the last of the block's CTAs to arrive, gather all
     // partials in fixed CTA order and finish the block.
@@ -237,23 +240,22 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
     if (finalize) {
         const int b = si.b0 + blk;
         const uint2 sv = *reinterpret_cast<const uint2*>(p.g.svh[si.g] + b * 128 + 4 * lane);
-        // this CTA's k-range partial of the block, summed over the CTAs that shared it
-        auto block_sum = [&](int row, float (&v)[4]) {
+        // the partials of CTAs lo..hi-1 (in CTA order) of `row`, one batch of loads in flight at a time
+        auto run_sum = [&](int row, int lo, int hi, float (&v)[4]) {
             v[0] = v[1] = v[2] = v[3] = 0.f;
-            for (int c0 = cf; c0 <= cl; c0 += kMaxBatch) {
-                // all loads of a batch in flight together, then summed in CTA order
+            for (int c0 = lo; c0 < hi; c0 += kMaxBatch) {
                 float4 t[kMaxBatch];
 #pragma unroll
                 for (int q = 0; q < kMaxBatch; ++q) {
                     const int cc = c0 + q;
-                    if (cc > cl) break;
+                    if (cc >= hi) break;
                     t[q] = (cc == c) ? *reinterpret_cast<const float4*>(acc_s + row * kAccCols + col)
                                      : __ldcg(reinterpret_cast<const float4*>(
                                            p.partials + ((int64_t)(cc + sb) * m + row) * p.sb_cols + col));
                 }
 #pragma unroll
                 for (int q = 0; q < kMaxBatch; ++q) {
-                    if (c0 + q > cl) break;
+                    if (c0 + q >= hi) break;
                     v[0] += t[q].x; v[1] += t[q].y; v[2] += t[q].z; v[3] += t[q].w;
                 }
             }
@@ -281,12 +283,61 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
             }
             *dst = make_uint2(h2_as_u32(y01), h2_as_u32(y23));
         };
-        if (p.tp_size <= 1) {
-            for (int row = r_lo; row < r_hi; ++row) {
-                float v[4];
-                block_sum(row, v);
+        // Exchange (tensor parallel): this rank's k-slice partial of block b goes to every rank as
+        // (value, call) pairs in slot [par][rank][b] of each rank's buffer; then each rank polls its
+        // own slots of every rank until all pairs carry this call's number, and sums in rank order.
+        const int tp = p.tp_size, rk = p.tp_rank, nb = p.tp_blocks, rows = p.tp_rows;
+        // the counter is written only by earlier kernels on this GPU (visible after griddepcontrol.wait)
+        const int ep = tp > 1 ? *reinterpret_cast<volatile const int*>(p.tp_buf[rk]) + 1 : 0;
+        const int par = ep & 1;
+        auto slot = [&](int owner, int src, int row) {
+            return reinterpret_cast<uint32_t*>(p.tp_buf[owner] + kTpHeader) +
+                   ((((int64_t)par * tp + src) * nb + b) * rows + row) * 256 + 8 * lane;
+        };
+        // the block's k-range sum of a row, over the CTAs that shared it, then its output (or, under
+        // tensor parallelism, its exchange)
+        auto consume = [&](int row, const float (&v)[4]) {
+            if (tp <= 1) {
                 finish_row(row, v);
+            } else {
+                for (int r = 0; r < tp; ++r) {
+                    uint32_t* d = slot(r, rk, row);
+                    st_pairs(d, v[0], v[1], ep);
+                    st_pairs(d + 4, v[2], v[3], ep);
+                }
             }
+        };
+        // The sum runs: m == 1: half h sums run h of row 0 (half 1's through hi_s); m > 1: each warp
+        // both runs of its rows.  One call site of run_sum for all of them.
+        const int mid = cf + (cl - cf + 2) / 2;  // runs cf..mid-1 and mid..cl (the second empty when whole)
+        float4* hi_mine = reinterpret_cast<float4*>(hi_s + blk * 128) + lane;
+        const int jobs = m == 1 ? 1 : 2 * (r_hi - r_lo);
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int it = 0; it < jobs; ++it) {
+            const int row = m == 1 ? 0 : r_lo + (it >> 1);
+            const int run = m == 1 ? half : (it & 1);
+            float w[4];
+            run_sum(row, run ? mid : cf, run ? cl + 1 : mid, w);
+            if (run == 0) {
+                v[0] = w[0]; v[1] = w[1]; v[2] = w[2]; v[3] = w[3];
+            } else if (m == 1) {
+                *hi_mine = make_float4(w[0], w[1], w[2], w[3]);
+            } else {
+                if (mid <= cl) { v[0] += w[0]; v[1] += w[1]; v[2] += w[2]; v[3] += w[3]; }
+                consume(row, v);
+            }
+        }
+        if (m == 1) {
+            pair_sync();  // half 1's run sum before half 0 reads it
+            if (half == 0) {
+                if (mid <= cl) {
+                    const float4 h = *hi_mine;
+                    v[0] += h.x; v[1] += h.y; v[2] += h.z; v[3] += h.w;
+                }
+                consume(0, v);
+            }
+        }
+        if (tp <= 1) {
             if (p.act) {
                 // gate and up block b are finished by different warp pairs, in any order: the
                 // second one (pair counter) reads both staged blocks and writes the activation
@@ -319,26 +370,6 @@ __device__ __forceinline__ void flush_block(const GemvParams& p, const float* ac
                 }
             }
         } else {
-            // Exchange this rank's k-slice partial of block b with every rank: (value, call) pairs
-            // into slot [par][rank][b] of each rank's buffer; then poll our own slots of every rank
-            // until all pairs carry this call's number, and sum in rank order.
-            const int tp = p.tp_size, rk = p.tp_rank, nb = p.tp_blocks, rows = p.tp_rows;
-            // the counter is written only by earlier kernels on this GPU (visible after griddepcontrol.wait)
-            const int ep = *reinterpret_cast<volatile const int*>(p.tp_buf[rk]) + 1;
-            const int par = ep & 1;
-            auto slot = [&](int owner, int src, int row) {
-                return reinterpret_cast<uint32_t*>(p.tp_buf[owner] + kTpHeader) +
-                       ((((int64_t)par * tp + src) * nb + b) * rows + row) * 256 + 8 * lane;
-            };
-            for (int row = r_lo; row < r_hi; ++row) {
-                float v[4];
-                block_sum(row, v);
-                for (int r = 0; r < tp; ++r) {
-                    uint32_t* d = slot(r, rk, row);
-                    st_pairs(d, v[0], v[1], ep);
-                    st_pairs(d + 4, v[2], v[3], ep);
-                }
-            }
             bool ok = true;
             for (int row = r_lo; row < r_hi; ++row) {
                 float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -572,6 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     }
 
     float* acc_s = reinterpret_cast<float*>(smem + lay.acc_off);
+    float* hi_s = reinterpret_cast<float*>(smem + lay.hi_off);
 
     // ------------------------------ decode warps ------------------------------
     if (p.norm_w) {  // the fused RMSNorm's row sums, shared with the producer
@@ -717,8 +749,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         named_bar(kFlushBar, kDecodeWarps * 32);
         {
             const int fb = warp & 7, half = warp >> 3;
-            if (fb < si.nblk && (half == 0 || m > 1) && *flush_snap == 0)
-                flush_block<MT>(p, acc_s, abort_flag, c, sb, si, fb, half, u0, u1, lane, fin_s + fb);
+            if (fb < si.nblk && *flush_snap == 0)
+                flush_block<MT>(p, acc_s, hi_s, abort_flag, c, sb, si, fb, half, u0, u1, lane, fin_s + fb);
         }
         if (i + 1 < nunits) {
             ++sb;
