@@ -47,7 +47,7 @@ L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gemv_kernel launch of the gate_up
 # call at K = 4, m = 1 on one GPU, from one ncu capture.  A capture describes the kernel source it was
 # taken from: the figure is reported only while the GEMV sources hash to src_sha256, else null.
-GEMV_TRAFFIC = {"src_sha256": "0e59988363e94da3f4ef6aa3a68f9c8fabba1855e588f773d27b738217cee40b", "bytes": 92646656}
+GEMV_TRAFFIC = {"src_sha256": "21ad7da65f2c47d3f7366a64bc4b5f81466e75f40a268e6243c7d9aa20189913", "bytes": 91791104}
 
 
 def gemv_source_sha() -> str:
@@ -429,7 +429,15 @@ def _event_ms(torch, fn, iters, flush=None):
     return statistics.median(times)
 
 
-def bench_prefill(torch, dev, K: int, m: int = 2048, iters: int = 10, peak_tflops: float = 1664.8) -> dict:
+def _measured_peaks() -> dict:
+    """The pool's measured peaks (MEASURED_PEAKS.json), {} when absent."""
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return {}
+
+
+def bench_prefill(torch, dev, K: int, m: int = 2048, iters: int = 10, peak_tflops: float = 1590.0) -> dict:
     """One gate_up-shaped EXL3 linear (5120 -> 17408) at M rows through the public op (the tcgen05 GEMM
     of exl3b_gemm: had_in, then the trellis decoded into shared memory feeding tcgen05.mma), with the
     L2 flushed before every call.  Beside it, the reference's own route on this GPU's libraries
@@ -748,7 +756,8 @@ def main():
         elif kind == "ceiling":
             rec = bench_decode_ceiling(torch, dev, int(a[0]), reps=args.steps)
         elif kind == "prefill":
-            rec = bench_prefill(torch, dev, int(a[0]), m=int(a[1]) if len(a) > 1 else 2048, iters=args.steps)
+            rec = bench_prefill(torch, dev, int(a[0]), m=int(a[1]) if len(a) > 1 else 2048, iters=args.steps,
+                                peak_tflops=float(_measured_peaks().get("bf16_tflops", 1590.0)))
         else:
             raise SystemExit(f"unknown leg {kind}")
         print(json.dumps({"only": args.only, **rec}))
