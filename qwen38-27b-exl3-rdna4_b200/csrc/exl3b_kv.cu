@@ -225,6 +225,30 @@ EXL3B_DEV float row_sum4(float v) {  // the xor-2/1 levels between the row's fou
 // (whose rounding is <= 0) clamps to 0 either way
 EXL3B_DEV float code_of(float v) { return fminf(fmaxf(floorf(__fadd_rn(v, 0.5f)), 0.f), 15.f); }
 
+// Two fp32 lanes in one 64-bit register pair (low = first) and the sm_100 packed fp32 arithmetic on
+// them (add / mul / fma .rn.f32x2): each lane is rounded exactly as the scalar .rn instruction.
+EXL3B_DEV uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+EXL3B_DEV void f2_unpack(uint64_t r, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r)); }
+EXL3B_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+EXL3B_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+EXL3B_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 __global__ void __launch_bounds__(256) kv_int4_write_kernel(const KvWriteArgs a, const KvInt4Extra x) {
     const int lane = threadIdx.x & 31, j = lane & 3;
     const int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kW4Rows + (lane >> 2);
@@ -314,11 +338,16 @@ __global__ void __launch_bounds__(256) kv_int4_write_kernel(const KvWriteArgs a,
         hi0 = fmaxf(hi0, __shfl_xor_sync(0xFFFFFFFFu, hi0, d));
     }
     const float mu = __fmul_rn(row_sum4(sum_chunks(cs)), 1.f / 128.f);
-    float ny[8][4];  // -y, the addend of every candidate's error
+    // chunks i and i + 1 side by side in one 64-bit register pair for the packed fp32 (f32x2)
+    // arithmetic of the search: each half rounds exactly as the scalar instruction would
+    uint64_t y2[4][4], ny2[4][4];  // y and -y (the addend of every candidate's error)
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) ny[i][c] = -y[i][c];
+        for (int c = 0; c < 4; ++c) {
+            y2[i][c] = f2_pack(y[2 * i][c], y[2 * i + 1][c]);
+            ny2[i][c] = f2_pack(-y[2 * i][c], -y[2 * i + 1][c]);
+        }
     float best_err = __int_as_float(0x7F800000), best_sc = 0.f, best_zp = 0.f;
 #pragma unroll 1
     for (int cand = 0; cand < kClipSteps * kClipSteps; ++cand) {
@@ -329,16 +358,23 @@ __global__ void __launch_bounds__(256) kv_int4_write_kernel(const KvWriteArgs a,
         const float sc = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 15.f), 1e-6f);
         const float zp = code_of(__fdiv_rn(-lo, sc));
         const float inv = __fdiv_rn(1.f, sc);
+        const uint64_t inv2 = f2_pack(inv, inv), zp2 = f2_pack(zp, zp), nzp2 = f2_pack(-zp, -zp);
+        const uint64_t sc2 = f2_pack(sc, sc), half2 = f2_pack(0.5f, 0.5f);
+        // per element, as the scalar code_of / error: e = (code_of(y * inv + zp) - zp) * sc - y, and
+        // the chunk's sum of e^2 in element order; code_of's floor and clamp stay scalar
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            float e[4];
+        for (int i = 0; i < 4; ++i) {
+            uint64_t q2 = 0;
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                e[c] = __fmaf_rn(code_of(__fmaf_rn(y[i][c], inv, zp)) - zp, sc, ny[i][c]);
-            float q = __fmul_rn(e[0], e[0]);
-            q = __fmaf_rn(e[1], e[1], q);
-            q = __fmaf_rn(e[2], e[2], q);
-            cs[i] = __fmaf_rn(e[3], e[3], q);
+            for (int c = 0; c < 4; ++c) {
+                float u0, u1;
+                f2_unpack(f2_add(f2_fma(y2[i][c], inv2, zp2), half2), u0, u1);
+                u0 = fminf(fmaxf(floorf(u0), 0.f), 15.f);
+                u1 = fminf(fmaxf(floorf(u1), 0.f), 15.f);
+                const uint64_t e2 = f2_fma(f2_add(f2_pack(u0, u1), nzp2), sc2, ny2[i][c]);
+                q2 = c == 0 ? f2_mul(e2, e2) : f2_fma(e2, e2, q2);
+            }
+            f2_unpack(q2, cs[2 * i], cs[2 * i + 1]);
         }
         const float err = row_sum4(sum_chunks(cs));
         if (err < best_err) { best_err = err; best_sc = sc; best_zp = zp; }
